@@ -1,0 +1,129 @@
+"""In-tree build of the B200 SDPA forward (run from anywhere: ``python build.py [--force]``).
+
+Products (git-ignored, but they travel to the GPU box with the repository snapshot):
+
+* ``fused_attn/libfa_sm100.so`` -- the C-ABI library of include/fa_sm100.h: the sm_100a kernel
+  (csrc/fa_fwd_sm100.cu) and the dispatch layer (csrc/dispatch.cu), compiled by nvcc with
+  ``-gencode arch=compute_100a,code=sm_100a -lineinfo`` and the CUDA runtime linked statically,
+  so the library loads with or without torch in the process.
+* ``fused_attn/_C<EXT_SUFFIX>`` -- the PyTorch operator library (csrc/ext.cpp), host C++ only,
+  linked against libfa_sm100.so through an ``$ORIGIN`` rpath.
+
+nvcc cross-compiles without a GPU, so this runs on the CPU build host too.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import shutil
+import subprocess
+import sys
+import sysconfig
+from pathlib import Path
+
+PKG_ROOT = Path(__file__).resolve().parent
+REPO_ROOT = PKG_ROOT.parent
+CSRC = PKG_ROOT / "csrc"
+OUT_DIR = PKG_ROOT / "fused_attn"
+BUILD_DIR = PKG_ROOT / "_build"
+INCLUDE = REPO_ROOT / "include"
+
+CUDA_HOME = Path(os.environ.get("CUDA_HOME", "/usr/local/cuda"))
+NVCC = str(CUDA_HOME / "bin" / "nvcc")
+ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = [*ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
+              "-Xcompiler", "-Wall", f"-I{INCLUDE}", f"-I{CSRC}"]
+
+KERNEL_SOURCES = ["fa_fwd_sm100.cu", "dispatch.cu"]
+KERNEL_HEADERS = ["sm100_ptx.cuh", "fa_launch.h"]
+
+LIB_NAME = "libfa_sm100.so"
+EXT_NAME = "_C" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so")
+
+
+def lib_path() -> Path:
+    return OUT_DIR / LIB_NAME
+
+
+def ext_path() -> Path:
+    return OUT_DIR / EXT_NAME
+
+
+def _stale(target: Path, deps: list[Path]) -> bool:
+    if not target.exists():
+        return True
+    t = target.stat().st_mtime
+    return any(d.stat().st_mtime > t for d in deps)
+
+
+def _run(cmd: list[str], verbose: bool) -> None:
+    if verbose:
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+
+
+def build_kernels(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> Path:
+    BUILD_DIR.mkdir(exist_ok=True)
+    headers = [CSRC / h for h in KERNEL_HEADERS] + [INCLUDE / "fa_sm100.h"]
+    objs = []
+    for src in KERNEL_SOURCES:
+        s = CSRC / src
+        o = BUILD_DIR / (s.stem + ".o")
+        if force or _stale(o, [s, *headers]):
+            extra = ["-Xptxas", "-v"] if ptxas_verbose else []
+            _run([NVCC, *NVCC_FLAGS, *extra, "-c", str(s), "-o", str(o)], verbose)
+        objs.append(o)
+    lib = lib_path()
+    if force or _stale(lib, objs):
+        _run([NVCC, *ARCH_FLAGS, "-shared", "-Xlinker", f"-soname={LIB_NAME}", "-o", str(lib),
+              *map(str, objs)], verbose)
+    return lib
+
+
+def build_ext(force: bool = False, verbose: bool = False) -> Path:
+    import torch
+    from torch.utils import cpp_extension
+
+    src = CSRC / "ext.cpp"
+    out = ext_path()
+    deps = [src, INCLUDE / "fa_sm100.h", lib_path()]
+    if not force and not _stale(out, deps):
+        return out
+    cxx = os.environ.get("CXX", shutil.which("g++") or "g++")
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    incs = [*cpp_extension.include_paths(), sysconfig.get_paths()["include"], str(CUDA_HOME / "include"),
+            str(INCLUDE)]
+    libdirs = cpp_extension.library_paths()
+    cmd = [cxx, "-O2", "-std=c++17", "-fPIC", "-shared", "-Wall", "-Wno-unused-parameter",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}", "-DTORCH_EXTENSION_NAME=_C",
+           *(f"-I{i}" for i in incs), str(src), "-o", str(out),
+           *(f"-L{d}" for d in libdirs), "-lc10", "-lc10_cuda", "-ltorch", "-ltorch_cpu",
+           "-ltorch_cuda", f"-L{OUT_DIR}", "-l:" + LIB_NAME, "-Wl,-rpath,$ORIGIN"]
+    _run(cmd, verbose)
+    return out
+
+
+def build(force: bool = False, verbose: bool = False, ext: bool = True) -> None:
+    build_kernels(force=force, verbose=verbose)
+    if ext:
+        build_ext(force=force, verbose=verbose)
+
+
+def main(argv: list[str] | None = None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--force", action="store_true", help="rebuild everything")
+    ap.add_argument("--no-ext", action="store_true", help="only the C-ABI library")
+    ap.add_argument("--ptxas-verbose", action="store_true", help="print registers/spills")
+    ap.add_argument("-v", "--verbose", action="store_true")
+    args = ap.parse_args(argv)
+    build_kernels(force=args.force or args.ptxas_verbose, verbose=args.verbose,
+                  ptxas_verbose=args.ptxas_verbose)
+    if not args.no_ext:
+        build_ext(force=args.force, verbose=args.verbose)
+    print(f"built {lib_path()}" + ("" if args.no_ext else f" and {ext_path()}"))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

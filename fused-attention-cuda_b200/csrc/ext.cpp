@@ -1,0 +1,216 @@
+// fused_attn._C -- PyTorch operator surface over the C ABI in include/fa_sm100.h.
+//
+// Reference counterpart: python/fused_attn/ext.cpp.  Same library name (fused_attn), same
+// validation messages (make_params, ext.cpp:82-126), same bare PyInit__C module (ext.cpp:240-253)
+// so `from . import _C` runs the TORCH_LIBRARY initialisers.  One deliberate change:
+//   fused_attn::forward(Tensor q, Tensor k, Tensor v, bool is_causal, float scale)
+//       -> (Tensor, Tensor)                           (O, LSE) -- the reference returns O only
+// because the B200 build's contract is "forward -> (O, LSE)".  forward_stage keeps its
+// (Tensor, Tensor) schema; its LSE is empty for the stages that do not write one (1, 2).
+//
+// Host C++ only: every launch happens behind fa_forward() in libfa_sm100.so.
+#include <Python.h>  // first, per the CPython docs
+// (blank comment line keeps include sorters from moving Python.h)
+
+#include <ATen/ATen.h>
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAFunctions.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+#include <torch/library.h>
+
+#include <cmath>
+#include <cstdint>
+#include <limits>
+#include <string>
+#include <tuple>
+
+#include "fa_sm100.h"
+
+namespace {
+
+constexpr int64_t kMinStage = 1;
+constexpr int64_t kMaxStage = 5;
+constexpr int64_t kFirstLseStage = 3;
+
+int to_fa_dtype(at::ScalarType t) {
+  if (t == at::kFloat) return FA_DTYPE_F32;
+  if (t == at::kHalf) return FA_DTYPE_F16;
+  TORCH_CHECK(t == at::kBFloat16, "fused_attn: unsupported dtype ", t,
+              " (supported: float32, float16, bfloat16)");
+  return FA_DTYPE_BF16;
+}
+
+int dtype_from_name(const std::string& name) {
+  if (name == "fp32") return FA_DTYPE_F32;
+  if (name == "fp16") return FA_DTYPE_F16;
+  TORCH_CHECK(name == "bf16", "fused_attn: unknown dtype name '", name,
+              "' (expected fp32, fp16 or bf16)");
+  return FA_DTYPE_BF16;
+}
+
+int current_sm() {
+  const cudaDeviceProp* prop = at::cuda::getCurrentDeviceProperties();
+  return prop->major * 10 + prop->minor;
+}
+
+void check_stage(int64_t stage) {
+  TORCH_CHECK(stage >= kMinStage && stage <= kMaxStage, "fused_attn: stage must be in 1..5, got ",
+              stage);
+}
+
+int checked_int(int64_t v, const char* what) {
+  TORCH_CHECK(v >= 0 && v <= std::numeric_limits<int>::max(), "fused_attn: ", what, "=", v,
+              " does not fit fa_params_t (int)");
+  return static_cast<int>(v);
+}
+
+// Input contract (reference ext.cpp:82-126): every violation is a RuntimeError, never a fault.
+fa_params_t make_params(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                        bool is_causal, double scale) {
+  TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda(),
+              "fused_attn: q, k, v must be CUDA tensors");
+  TORCH_CHECK(q.device() == k.device() && q.device() == v.device(),
+              "fused_attn: q, k, v must live on the same device");
+  TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4,
+              "fused_attn: q, k, v must be [B, H, N, D]; got ", q.dim(), "-D, ", k.dim(), "-D, ",
+              v.dim(), "-D");
+  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous(),
+              "fused_attn: q, k, v must be contiguous [B, H, N, D] (call .contiguous())");
+  for (const at::Tensor* t : {&q, &k, &v}) {
+    TORCH_CHECK(reinterpret_cast<std::uintptr_t>(t->data_ptr()) % 16 == 0,
+                "fused_attn: q/k/v must be 16-byte aligned (use a fresh contiguous tensor)");
+  }
+  TORCH_CHECK(q.scalar_type() == k.scalar_type() && q.scalar_type() == v.scalar_type(),
+              "fused_attn: q, k, v must share one dtype; got ", q.scalar_type(), ", ",
+              k.scalar_type(), ", ", v.scalar_type());
+  (void)to_fa_dtype(q.scalar_type());
+
+  const int64_t B = q.size(0), H = q.size(1), N = q.size(2), D = q.size(3);
+  const int64_t Hkv = k.size(1);
+  TORCH_CHECK(k.size(0) == B && v.size(0) == B, "fused_attn: batch mismatch between q, k, v");
+  TORCH_CHECK(v.size(1) == Hkv, "fused_attn: k and v must have the same number of heads");
+  TORCH_CHECK(k.size(2) == N && v.size(2) == N,
+              "fused_attn: Nq == Nkv is required in-window (got Nq=", N, ", Nkv=", k.size(2), ")");
+  TORCH_CHECK(k.size(3) == D && v.size(3) == D, "fused_attn: head-dim mismatch between q, k, v");
+  TORCH_CHECK(D == 64 || D == 128, "fused_attn: D must be 64 or 128, got ", D);
+  TORCH_CHECK(N % 32 == 0, "fused_attn: N must be a multiple of 32, got ", N,
+              " (ragged sequence lengths are a stated in-window limitation)");
+  TORCH_CHECK(Hkv >= 1 && H % Hkv == 0, "fused_attn: H=", H, " must be a multiple of Hkv=", Hkv);
+  TORCH_CHECK(scale > 0.0 && std::isfinite(scale), "fused_attn: scale must be finite and > 0, got ",
+              scale);
+
+  fa_params_t p;
+  p.B = checked_int(B, "B");
+  p.H = checked_int(H, "H");
+  p.Hkv = checked_int(Hkv, "Hkv");
+  p.N = checked_int(N, "N");
+  p.D = checked_int(D, "D");
+  p.scale = static_cast<float>(scale);
+  p.causal = is_causal ? 1 : 0;
+  return p;
+}
+
+std::tuple<at::Tensor, at::Tensor> run_stage(const at::Tensor& q, const at::Tensor& k,
+                                             const at::Tensor& v, bool is_causal, double scale,
+                                             int64_t stage) {
+  check_stage(stage);
+  const fa_params_t p = make_params(q, k, v, is_causal, scale);
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int impl = static_cast<int>(stage);
+  const int dtype = to_fa_dtype(q.scalar_type());
+  const int sm = current_sm();
+  TORCH_CHECK(fa_impl_supports(impl, dtype, p.D, sm), "fused_attn: stage ", stage, " (",
+              fa_impl_name(impl), ") is not implemented for ", fa_dtype_name(dtype), " D=", p.D,
+              " on sm_", sm);
+
+  at::Tensor o = at::empty_like(q);
+  const bool has_lse = stage >= kFirstLseStage;
+  at::Tensor lse = has_lse ? at::empty({p.B, p.H, p.N}, q.options().dtype(at::kFloat))
+                           : at::empty({0}, q.options().dtype(at::kFloat));
+  const std::size_t ws_bytes = fa_workspace_bytes(impl, dtype, &p);
+  at::Tensor workspace;
+  void* ws_ptr = nullptr;
+  if (ws_bytes > 0) {
+    workspace = at::empty({static_cast<int64_t>(ws_bytes)}, q.options().dtype(at::kByte));
+    ws_ptr = workspace.data_ptr();
+  }
+  const cudaStream_t stream = at::cuda::getCurrentCUDAStream(q.device().index()).stream();
+  const int err = fa_forward(impl, dtype, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                             has_lse ? lse.data_ptr<float>() : nullptr, ws_ptr, &p, stream);
+  TORCH_CHECK(err == 0, "fused_attn: stage ", stage, " (", fa_impl_name(impl),
+              ") failed: ", cudaGetErrorString(static_cast<cudaError_t>(err)));
+  return std::make_tuple(std::move(o), std::move(lse));
+}
+
+// forward: the highest stage that fa_impl_supports() accepts (reference ext.cpp:174-188).
+std::tuple<at::Tensor, at::Tensor> forward_cuda(const at::Tensor& q, const at::Tensor& k,
+                                                const at::Tensor& v, bool is_causal,
+                                                double scale) {
+  const fa_params_t p = make_params(q, k, v, is_causal, scale);
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int dtype = to_fa_dtype(q.scalar_type());
+  const int sm = current_sm();
+  for (int64_t stage = kMaxStage; stage >= kFirstLseStage; --stage) {
+    if (fa_impl_supports(static_cast<int>(stage), dtype, p.D, sm)) {
+      return run_stage(q, k, v, is_causal, scale, stage);
+    }
+  }
+  TORCH_CHECK(false, "fused_attn: no stage is implemented for ", fa_dtype_name(dtype), " D=", p.D,
+              " on sm_", sm);
+  return {};
+}
+
+std::tuple<at::Tensor, at::Tensor> forward_stage_cuda(const at::Tensor& q, const at::Tensor& k,
+                                                      const at::Tensor& v, bool is_causal,
+                                                      double scale, int64_t stage) {
+  return run_stage(q, k, v, is_causal, scale, stage);
+}
+
+void set_debug_overrides_op(int64_t block_m, int64_t block_n) {
+  fa_set_debug_overrides(checked_int(block_m, "block_m"), checked_int(block_n, "block_n"));
+}
+
+bool impl_supports_op(int64_t stage, std::string dtype, int64_t D) {
+  check_stage(stage);
+  if (c10::cuda::device_count() == 0) return false;
+  return fa_impl_supports(static_cast<int>(stage), dtype_from_name(dtype), checked_int(D, "D"),
+                          current_sm()) != 0;
+}
+
+std::string impl_name_op(int64_t stage) {
+  check_stage(stage);
+  return std::string(fa_impl_name(static_cast<int>(stage)));
+}
+
+}  // namespace
+
+TORCH_LIBRARY(fused_attn, m) {
+  m.def("forward(Tensor q, Tensor k, Tensor v, bool is_causal, float scale) -> (Tensor, Tensor)");
+  m.def(
+      "forward_stage(Tensor q, Tensor k, Tensor v, bool is_causal, float scale, int stage)"
+      " -> (Tensor, Tensor)");
+  m.def("set_debug_overrides(int block_m, int block_n) -> ()", &set_debug_overrides_op);
+  m.def("impl_supports(int stage, str dtype, int D) -> bool", &impl_supports_op);
+  m.def("impl_name(int stage) -> str", &impl_name_op);
+}
+
+TORCH_LIBRARY_IMPL(fused_attn, CUDA, m) {
+  m.impl("forward", &forward_cuda);
+  m.impl("forward_stage", &forward_stage_cuda);
+}
+
+extern "C" PyObject* PyInit__C(void) {
+  static struct PyModuleDef module_def = {
+      PyModuleDef_HEAD_INIT,
+      "_C",
+      "fused-attention B200 extension. The ops live in torch.ops.fused_attn.*",
+      -1,
+      nullptr,
+      nullptr,
+      nullptr,
+      nullptr,
+      nullptr,
+  };
+  return PyModule_Create(&module_def);
+}

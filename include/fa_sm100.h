@@ -1,0 +1,103 @@
+/* fa_sm100.h -- C ABI of the B200 (sm_100a) fused SDPA forward.
+ *
+ * This is the drop-in boundary.  Every entry point replaces one function of the reference's
+ * frozen C++ kernel API, include/fa/attention.cuh (yashpatil582/fused-attention-cuda), with
+ * the same argument meaning, the same layout contract and the same error convention, flattened
+ * to `extern "C"` with plain pointers, ints and a POD struct so that ctypes / cgo / JNI / N-API
+ * can bind it without C++ name mangling or torch types.
+ *
+ * Layout contract (attention.cuh:38-40): q, o are [B, H, N, D]; k, v are [B, Hkv, N, D]; all
+ * contiguous with D fastest, 16-byte aligned; lse is [B, H, N] fp32, natural-log logsumexp of
+ * the scaled scores per query row (m*scale + ln l; +inf for a row that sees no key).
+ * Causal masks are top-left aligned (key j visible to query i iff j <= i), Nq == Nkv.
+ *
+ * Error convention (attention.cuh:43-45, src/dispatch.cu:96-111): functions return a
+ * cudaError_t value as int and never abort; cudaErrorInvalidValue (1) for bad parameters,
+ * cudaErrorNotSupported (801) when (impl, dtype, D, device) is not built.  Launches are
+ * asynchronous on the caller's stream and never synchronise.  Messages go to stderr only when
+ * FA_VERBOSE is set.  Device-side bounded waits report through fa_last_device_error().
+ *
+ * Threading: the debug overrides and the wait-time limit are process-global and not
+ * thread-safe (as g_overrides in src/dispatch.cu:136).
+ */
+#ifndef FA_SM100_H_
+#define FA_SM100_H_
+
+#include <cuda_runtime_api.h>
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element type of q/k/v/o -- fa::Dtype (attention.cuh:17). */
+enum fa_dtype { FA_DTYPE_F32 = 0, FA_DTYPE_F16 = 1, FA_DTYPE_BF16 = 2 };
+
+/* Implementation id -- fa::Impl (attention.cuh:20-26).  This build implements FA_IMPL_TUNED
+ * only, and on B200 it is the tcgen05/TMA kernel; the reference's teaching rungs 1-4 report
+ * cudaErrorNotSupported. */
+enum fa_impl {
+  FA_IMPL_NAIVE = 1,
+  FA_IMPL_TILED = 2,
+  FA_IMPL_FUSED = 3,
+  FA_IMPL_WMMA = 4,
+  FA_IMPL_TUNED = 5
+};
+
+/* fa::Params (attention.cuh:28-36); `causal` is an int instead of a C++ bool. */
+typedef struct fa_params {
+  int B;       /* batch */
+  int H;       /* query heads */
+  int Hkv;     /* key/value heads, H % Hkv == 0 */
+  int N;       /* sequence length (Nq == Nkv), N % 32 == 0 */
+  int D;       /* head dim, 64 or 128 */
+  float scale; /* softmax scale, finite and > 0 (PyTorch default 1/sqrt(D)) */
+  int causal;  /* 0/1, top-left aligned */
+} fa_params_t;
+
+/* fa::forward (attention.cuh:46-47; implementation src/dispatch.cu:140-161).
+ * Launches the fused forward on `stream`.  `workspace` may be NULL (fa_workspace_bytes is 0). */
+int fa_forward(int impl, int dtype, const void* q, const void* k, const void* v, void* o,
+               float* lse, void* workspace, const fa_params_t* p, cudaStream_t stream);
+
+/* fa::workspace_bytes (attention.cuh:51; src/dispatch.cu:163-168).  0 for the fused kernel. */
+size_t fa_workspace_bytes(int impl, int dtype, const fa_params_t* p);
+
+/* fa::impl_supports (attention.cuh:56; src/dispatch.cu:170-175).  `sm` = major*10+minor. */
+int fa_impl_supports(int impl, int dtype, int D, int sm);
+
+/* fa::set_debug_overrides / get_debug_overrides (attention.cuh:60-66; src/dispatch.cu:177-189).
+ * block_m: 0 or 128 (query rows per tile); block_n: 0, 32, 64 or 128 (keys per tile).
+ * Other values make fa_forward return cudaErrorInvalidValue, like the reference's
+ * non-instantiated variants (src/stage5_tuned.cu:934-950).  With from_env != 0 the
+ * FA_FORCE_BR / FA_FORCE_BC environment variables override the stored values. */
+void fa_set_debug_overrides(int block_m, int block_n);
+void fa_get_debug_overrides(int from_env, int* block_m, int* block_n);
+
+/* fa::impl_name / dtype_name / dtype_size (attention.cuh:67-69; src/dispatch.cu:191-230). */
+const char* fa_impl_name(int impl);
+const char* fa_dtype_name(int dtype);
+size_t fa_dtype_size(int dtype);
+
+/* No counterpart in the reference (its kernels never wait on anything).  Every mbarrier wait
+ * in the sm_100a kernel is bounded; a wait that runs out records a cause bit in a device-side
+ * status word, the kernel drains its own copies, frees its tensor memory and exits normally.
+ * This call synchronises the current device, returns cudaErrorLaunchTimeout (702) if any
+ * launch since the previous call timed out (else the device's sticky error, or cudaSuccess),
+ * stores the cause bits in *detail when detail != NULL, and clears the status word. */
+int fa_last_device_error(unsigned int* detail);
+
+/* No counterpart in the reference: the time limit of each device-side wait, in nanoseconds
+ * (default 2e9).  Used by the failure-detection tests to make an injected stall end quickly. */
+void fa_set_wait_timeout_ns(unsigned long long ns);
+
+/* No counterpart in the reference: test-only fault injection on the host side of the launch.
+ * When tile >= 0, the producer warp of every CTA skips the K load of key tile `tile`, so the
+ * MMA warp's bounded wait for it runs out (no GPU fault, no trap).  -1 disables. */
+void fa_debug_set_skip_kv_tile(int tile);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FA_SM100_H_ */
