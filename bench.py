@@ -1,0 +1,534 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 SDPA forward -- prints ONE JSON line (rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload C3]
+
+Metric (the benchmark baseline's): SDPA forward TFLOP/s (4*B*H*N^2*D FLOPs, halved for causal)
+and ms per step, against the measured B200 dense bf16/fp16 tensor peak.  A step is one forward
+pass over one batch of seeded synthetic inputs (torch.randn iid N(0,1), the reference's
+generator).  Default workload: C3 = B2 H8 N2048 D128 fp16 top-left causal, seed 2.
+
+* ``value``       device time of the kernel alone (CUDA events on the launching stream, one
+                  pair per step), inputs resident in HBM, L2 flushed (256 MiB write) before
+                  every timed launch; whole-job FLOPs / max-over-ranks time.
+* ``e2e``         the same metric through the public op (torch.ops.fused_attn.forward) with
+                  pinned HOST buffers: q/k/v copied in and O/LSE copied out inside every step.
+* ``roofline``    tensor-bound: achieved TFLOP/s of the kernel / measured bf16 peak
+                  (MEASURED_PEAKS.json, burst figure: the kernel is timed alone).  ``traffic``
+                  is the per-launch DRAM bytes of the committed ncu summary for this workload.
+* ``cpu_baseline`` the reference's own fp64 CPU oracle (oracle/_ref, else the C restatement) on
+                  a bounded sample of the workload, on this host's cores (rank 0, N=1 only).
+
+Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): one process per GPU, weak scaling:
+rank r runs the same per-GPU workload on its own shard of a global batch of N x B (seed + r), no
+collective on the data path; NCCL only reduces the per-rank device time (max) off the hot path.
+``--workload C4`` instead splits C4's 32 heads of one N=16384 sequence across the ranks (strong
+scaling, the long-context configuration).
+
+``--impl reference``: the reference's CPU implementation of the path (its fp64 oracle, which is
+the only implementation of the path that runs on this machine class besides ours) on the host
+cores, on the same workload/metric, each step a bounded sample (one (b, h) head).
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "fused-attention-cuda_b200"))
+
+METRIC = "SDPA fwd ms & TFLOP/s, B2H8N2048 D64/128 fp16, % of B200 tensor peak"
+UNIT = "TFLOP/s"
+FLUSH_BYTES = 256 << 20  # >= 2x the 126 MB L2
+FALLBACK_PEAK_TFLOPS = 1590.0
+
+
+def env_int(name: str, default: int) -> int:
+    try:
+        return int(os.environ.get(name, default))
+    except ValueError:
+        return default
+
+
+def load_peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        d = json.loads(p.read_text())
+        return float(d["bf16_tflops"]), "measured (MEASURED_PEAKS.json bf16_tflops, burst)"
+    except Exception:
+        return FALLBACK_PEAK_TFLOPS, "fallback 1.59 PFLOP/s (MEASURED_PEAKS.json absent)"
+
+
+def profile_traffic(workload: str) -> int | None:
+    """Per-launch DRAM bytes from the committed ncu summary (profiles/), if one exists."""
+    for f in sorted((ROOT / "profiles").glob("*.txt")):
+        try:
+            text = f.read_text()
+        except OSError:
+            continue
+        if f"workload: {workload}" not in text:
+            continue
+        for line in text.splitlines():
+            if line.startswith("dram_bytes_per_launch:"):
+                try:
+                    return int(float(line.split(":", 1)[1].split()[0]))
+                except ValueError:
+                    return None
+    return None
+
+
+# ------------------------------------------------------------------------------------------
+class ClockSampler:
+    """nvidia-smi SM clock / throttle-reason sampler around the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.samples: list[tuple[float, list[str]]] = []
+        self.proc = None
+        self.thread = None
+        self.t0 = self.t1 = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), [x.strip() for x in line.split(",")]))
+
+    def window(self, t0: float, t1: float) -> None:
+        self.t0, self.t1 = t0, t1
+
+    def stop(self) -> dict | None:
+        if self.proc is None:
+            return None
+        time.sleep(0.15)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        inside = [s for t, s in self.samples if self.t0 is not None and self.t0 <= t <= self.t1]
+        use = inside or [s for _, s in self.samples]
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for s in use:
+            try:
+                sm.append(float(s[1]))
+                mx.append(float(s[2]))
+            except (ValueError, IndexError):
+                continue
+            for n, val in zip(names, s[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(use), "samples_in_timed_region": len(inside)}
+
+
+# ------------------------------------------------------------------------------------------
+def workload_config(name: str):
+    from fused_attn.workloads import CONFIGS
+
+    key = {"c2": "C2", "c2c": "C2c", "c3": "C3", "c3bf16": "C3bf16", "c4": "C4"}.get(name.lower())
+    if key is None:
+        raise SystemExit(f"unknown workload {name}")
+    return CONFIGS[key]
+
+
+def time_kernel(fn, steps: int, warmup: int, flush, stream) -> list[float]:
+    """Per-step device times (ms) of fn() on `stream`, L2 flushed before every launch."""
+    import torch
+
+    for _ in range(warmup):
+        flush.zero_()
+        fn()
+    torch.cuda.synchronize()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    for i in range(steps):
+        flush.zero_()  # queued first: the GPU is busy while the host enqueues the launch
+        starts[i].record(stream)
+        fn()
+        ends[i].record(stream)
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in zip(starts, ends)]
+
+
+def cpu_sample(cfg, budget_s: float, threads: int) -> dict:
+    """Times the reference's fp64 oracle on whole (b, h) heads of `cfg` until `budget_s`."""
+    import oracle
+    from fused_attn.workloads import attention_flops, make_qkv
+
+    kind = "reference" if oracle.ref_available() else "port"
+    heads_done, flops, elapsed = 0, 0.0, 0.0
+    total_heads = cfg.B * cfg.H
+    q, k, v = make_qkv(cfg.B, cfg.H, cfg.N, cfg.D, dtype=cfg.dtype, hkv=cfg.hkv, seed=cfg.seed)
+    while heads_done < total_heads and elapsed < budget_s:
+        b, h = divmod(heads_done, cfg.H)
+        qs, ks, vs = q[b:b + 1, h:h + 1], k[b:b + 1, h:h + 1], v[b:b + 1, h:h + 1]
+        qs, ks, vs = (t.double().contiguous() for t in (qs, ks, vs))
+        t0 = time.perf_counter()
+        if kind == "reference":
+            _, _, used = oracle.ref_attention(qs, ks, vs, causal=cfg.causal, threads=threads)
+        else:
+            oracle.attention(qs, ks, vs, causal=cfg.causal, threads=threads)
+            used = threads
+        elapsed += time.perf_counter() - t0
+        flops += attention_flops(1, 1, cfg.N, cfg.D, cfg.causal)
+        heads_done += 1
+    return {"value": flops / elapsed / 1e12, "unit": UNIT, "cores": threads, "kind": kind,
+            "sample": f"{heads_done} of {total_heads} (b,h) heads of {cfg.label()}, fp64, "
+                      f"{elapsed:.1f} s, rows split over {threads} threads",
+            "ms_per_head": 1e3 * elapsed / max(heads_done, 1)}
+
+
+# ------------------------------------------------------------------------------------------
+def run_reference(args) -> int:
+    """--impl reference: the reference's CPU implementation of the path (rank 0 only)."""
+    if env_int("RANK", 0) != 0:
+        return 0
+    sys.path.insert(0, str(ROOT))
+    import oracle
+    from fused_attn.workloads import attention_flops, make_qkv
+
+    cfg = workload_config(args.workload)
+    threads = oracle.default_threads()
+    kind = "reference" if oracle.ref_available() else "port"
+    q, k, v = make_qkv(cfg.B, cfg.H, cfg.N, cfg.D, dtype=cfg.dtype, hkv=cfg.hkv, seed=cfg.seed)
+    heads = [(b, h) for b in range(cfg.B) for h in range(cfg.H)]
+
+    def step(i):
+        b, h = heads[i % len(heads)]
+        qs, ks, vs = (t[b:b + 1, h:h + 1].double().contiguous() for t in (q, k, v))
+        if kind == "reference":
+            oracle.ref_attention(qs, ks, vs, causal=cfg.causal, threads=threads)
+        else:
+            oracle.attention(qs, ks, vs, causal=cfg.causal, threads=threads)
+
+    for i in range(args.warmup):
+        step(i)
+    times = []
+    for i in range(args.steps):
+        t0 = time.perf_counter()
+        step(args.warmup + i)
+        times.append(time.perf_counter() - t0)
+    f_step = attention_flops(1, 1, cfg.N, cfg.D, cfg.causal)
+    value = f_step * len(times) / sum(times) / 1e12
+    dt = {"torch.float16": "fp16", "torch.bfloat16": "bf16"}.get(str(cfg.dtype), "fp32")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * sum(times) / len(times), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp64",
+        "data": f"synthetic: torch.randn seed {cfg.seed}, rounded to {dt}, upcast to fp64",
+        "config": {"workload": cfg.label(), "global_batch": cfg.B, "seq_len": cfg.N,
+                   "heads": cfg.H, "head_dim": cfg.D, "causal": cfg.causal,
+                   "step": "one (b, h) head of the workload (bounded sample)"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": "one (b, h) head per step, cycling through the heads"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args) -> int:
+    import torch
+    import torch.distributed as dist
+
+    import fused_attn
+    from fused_attn.workloads import Config, attention_bytes, attention_flops, make_qkv
+
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local_rank = env_int("LOCAL_RANK", 0)
+    if args.gpus != world and world > 1:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (the kernel has no CPU fallback)")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=180),
+                                device_id=dev)
+    if not fused_attn.is_available():
+        raise SystemExit("fused_attn._C is not built (python fused-attention-cuda_b200/build.py)")
+
+    base = workload_config(args.workload)
+    if base.name == "C4":
+        # Strong scaling: the 32 heads of one sequence split into contiguous per-rank blocks.
+        if base.H % world:
+            raise SystemExit(f"C4 has {base.H} heads, not divisible by {world}")
+        hs = base.H // world
+        q_all, k_all, v_all = make_qkv(base.B, base.H, base.N, base.D, dtype=base.dtype,
+                                       seed=base.seed)
+        sl = slice(rank * hs, (rank + 1) * hs)
+        q, k, v = (t[:, sl].contiguous().to(dev) for t in (q_all, k_all, v_all))
+        del q_all, k_all, v_all
+        cfg = Config("C4", base.B, hs, base.N, base.D, base.dtype, base.seed, base.causal)
+        scaling, global_batch = "strong", base.B
+        parallelism = f"head-sharded x{world} ({hs} heads/GPU), no collective"
+    else:
+        # Weak scaling: same per-GPU workload, rank r owns batch shard r (seed + r).
+        cfg = base
+        q, k, v = make_qkv(cfg.B, cfg.H, cfg.N, cfg.D, dtype=cfg.dtype, seed=cfg.seed + rank,
+                           device=dev)
+        scaling, global_batch = "weak", cfg.B * world
+        parallelism = f"batch-sharded dp{world}, no collective"
+
+    stream = torch.cuda.current_stream(dev)
+    flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    scale = 1.0 / math.sqrt(cfg.D)
+    op = torch.ops.fused_attn.forward
+
+    def fwd():
+        return op(q, k, v, cfg.causal, scale)
+
+    o, lse = fwd()
+    torch.cuda.synchronize()
+    err, bits = fused_attn.last_device_error()
+    if err != 0:
+        raise SystemExit(f"device status after the first launch: {err} bits={bits:#x}")
+
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(1.0)  # nvidia-smi start-up
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    t_wall0 = time.time()
+    times = time_kernel(fwd, args.steps, args.warmup, flush, stream)
+    torch.cuda.synchronize()
+    t_wall1 = time.time()
+    if world > 1:
+        dist.barrier()
+    if sampler:
+        sampler.window(t_wall0, t_wall1)
+
+    # ---- end to end through the public op, host buffers, copies inside every step -------
+    qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
+    oh = torch.empty(o.shape, dtype=o.dtype, pin_memory=True)
+    lh = torch.empty(lse.shape, dtype=lse.dtype, pin_memory=True)
+    qd, kd, vd = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+
+    def e2e_step():
+        qd.copy_(qh, non_blocking=True)
+        kd.copy_(kh, non_blocking=True)
+        vd.copy_(vh, non_blocking=True)
+        oo, ll = fused_attn.forward(qd, kd, vd, is_causal=cfg.causal, scale=scale, return_lse=True)
+        oh.copy_(oo, non_blocking=True)
+        lh.copy_(ll, non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 200))
+    for _ in range(max(1, min(args.warmup, 5))):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    clocks = sampler.stop() if sampler else None
+
+    err, bits = fused_attn.last_device_error()
+    if err != 0:
+        raise SystemExit(f"device status after timing: {err} bits={bits:#x}")
+
+    kernel_ms_sum = float(sum(times))
+    per_rank = torch.tensor([kernel_ms_sum, e2e_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(per_rank, op=dist.ReduceOp.MAX)
+    kernel_ms_sum, e2e_ms = float(per_rank[0]), float(per_rank[1])
+    ms_per_step = kernel_ms_sum / args.steps
+    flops_rank = attention_flops(cfg.B, cfg.H, cfg.N, cfg.D, cfg.causal)
+    flops_job = flops_rank * world
+    value = flops_job / (ms_per_step * 1e-3) / 1e12
+    e2e_value = flops_job / (e2e_ms * 1e-3) / 1e12
+
+    secondary = None
+    cpu_base = None
+    if rank == 0 and world == 1 and not args.quick:
+        secondary = secondary_measurements(cfg, q, k, v, flush, stream, max(20, min(args.steps, 200)))
+        cpu_base = cpu_sample(cfg, args.cpu_budget, threads=_host_threads())
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+
+    peak, peak_src = load_peaks()
+    achieved = flops_rank / (ms_per_step * 1e-3) / 1e12  # one launch on one GPU
+    dt = {torch.float16: "fp16", torch.bfloat16: "bf16"}[cfg.dtype]
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": UNIT,
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": scaling,
+        "vs_baseline": None,
+        "dtype": dt,
+        "data": f"synthetic: torch.randn iid N(0,1), seed {cfg.seed}(+rank), [B,H,N,D] contiguous",
+        "config": {
+            "workload": cfg.label() if base.name != "C4" else base.label(),
+            "global_batch": global_batch,
+            "seq_len": cfg.N,
+            "heads_per_gpu": cfg.H,
+            "head_dim": cfg.D,
+            "causal": cfg.causal,
+            "parallelism": parallelism,
+            "l2": "flushed before every timed launch (256 MiB write); inputs < L2",
+            "timing": "CUDA events per launch on the launching stream; max over ranks",
+        },
+        "roofline": {
+            "bound": "tensor",
+            "achieved": achieved,
+            "peak": peak,
+            "unit": "TFLOP/s",
+            "frac": achieved / peak,
+            "traffic": profile_traffic(base.name if base.name != "C3" else "C3"),
+            "peak_source": peak_src,
+            "algorithmic_bytes": attention_bytes(cfg.B, cfg.H, cfg.hkv, cfg.N, cfg.D, 2),
+            "algorithmic_flops": flops_rank,
+        },
+        "cpu_baseline": cpu_base,
+        "e2e": {
+            "value": e2e_value,
+            "unit": UNIT,
+            "h2d_bytes_per_step": int(sum(t.numel() * t.element_size() for t in (q, k, v))),
+            "d2h_bytes_per_step": int(o.numel() * o.element_size() + lse.numel() * lse.element_size()),
+            "ms_per_step": e2e_ms,
+            "steps": e2e_steps,
+            "api": "fused_attn.forward (torch.ops.fused_attn.forward) from pinned host memory",
+        },
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        "kernel_ms": {"median": statistics.median(times), "p10": _pct(times, 10),
+                      "p90": _pct(times, 90), "min": min(times)},
+        "secondary": secondary,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def _host_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def _pct(xs, p):
+    s = sorted(xs)
+    return s[min(len(s) - 1, max(0, int(round(p / 100 * (len(s) - 1)))))]
+
+
+def secondary_measurements(cfg, q, k, v, flush, stream, steps):
+    """Context numbers (not the headline): PyTorch SDPA on the same inputs and the same
+    protocol, a CUDA-graph batch average of our kernel, and the D64 (C2) configs."""
+    import torch
+    import torch.nn.functional as F
+
+    from fused_attn.workloads import CONFIGS, attention_flops, make_qkv
+
+    out = {}
+    fl = attention_flops(cfg.B, cfg.H, cfg.N, cfg.D, cfg.causal)
+    scale = 1.0 / math.sqrt(cfg.D)
+    t = time_kernel(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=cfg.causal),
+                    steps, 10, flush, stream)
+    ms = statistics.median(t)
+    out["torch_sdpa_same_gpu"] = {"ms_median": ms, "tflops": fl / ms / 1e9,
+                                  "note": "F.scaled_dot_product_attention default backend"}
+    t = time_kernel(lambda: torch.ops.fused_attn.forward(q, k, v, cfg.causal, scale), steps, 10,
+                    flush, stream)
+    ms = statistics.median(t)
+    out["ours_median"] = {"ms_median": ms, "tflops": fl / ms / 1e9}
+    # CUDA-graph batch of 20 launches (no flush in between: warm L2), labelled as such.
+    g = torch.cuda.CUDAGraph()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        torch.ops.fused_attn.forward(q, k, v, cfg.causal, scale)
+        with torch.cuda.graph(g, stream=s):
+            for _ in range(20):
+                torch.ops.fused_attn.forward(q, k, v, cfg.causal, scale)
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(5):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / 100
+    out["ours_cuda_graph_batch20_warm_l2"] = {"ms": ms, "tflops": fl / ms / 1e9}
+    del g
+    for name in ("C2", "C2c"):
+        c = CONFIGS[name]
+        q2, k2, v2 = make_qkv(c.B, c.H, c.N, c.D, dtype=c.dtype, seed=c.seed, device=q.device)
+        f2 = attention_flops(c.B, c.H, c.N, c.D, c.causal)
+        s2 = 1.0 / math.sqrt(c.D)
+        t = time_kernel(lambda: torch.ops.fused_attn.forward(q2, k2, v2, c.causal, s2), steps, 10,
+                        flush, stream)
+        ts = time_kernel(lambda: F.scaled_dot_product_attention(q2, k2, v2, is_causal=c.causal),
+                         steps, 10, flush, stream)
+        out[name] = {"workload": c.label(), "ours_ms": statistics.median(t),
+                     "ours_tflops": f2 / statistics.median(t) / 1e9,
+                     "sdpa_ms": statistics.median(ts), "sdpa_tflops": f2 / statistics.median(ts) / 1e9}
+    return out
+
+
+def main(argv=None) -> int:
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", default="C3", help="C3 (default), C3bf16, C2, C2c or C4")
+    ap.add_argument("--cpu-budget", type=float, default=12.0,
+                    help="seconds of CPU oracle work for the cpu_baseline sample")
+    ap.add_argument("--quick", action="store_true", help="skip secondary and CPU measurements")
+    args = ap.parse_args(argv)
+    args.warmup = max(args.warmup, 3)  # the timing rules require at least 3 warm-up steps
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

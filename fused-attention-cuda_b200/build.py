@@ -50,6 +50,19 @@ def ext_path() -> Path:
     return OUT_DIR / EXT_NAME
 
 
+def host_cxx() -> str:
+    """The host C++ compiler for the torch extension and for nvcc's host passes.
+
+    /usr/bin/g++ is preferred over $CXX: a wrapper compiler that redirects the crt/libgcc search
+    path (as this image's /opt/gcc/bin/g++ does) yields a library whose C++ exceptions crash
+    when a TORCH_CHECK unwinds through torch's dispatcher.  FA_HOST_CXX overrides both."""
+    for cand in (os.environ.get("FA_HOST_CXX"), "/usr/bin/g++", os.environ.get("CXX"),
+                 shutil.which("g++")):
+        if cand and Path(cand).exists():
+            return cand
+    return "g++"
+
+
 def _stale(target: Path, deps: list[Path]) -> bool:
     if not target.exists():
         return True
@@ -72,11 +85,12 @@ def build_kernels(force: bool = False, verbose: bool = False, ptxas_verbose: boo
         o = BUILD_DIR / (s.stem + ".o")
         if force or _stale(o, [s, *headers]):
             extra = ["-Xptxas", "-v"] if ptxas_verbose else []
-            _run([NVCC, *NVCC_FLAGS, *extra, "-c", str(s), "-o", str(o)], verbose)
+            _run([NVCC, "-ccbin", host_cxx(), *NVCC_FLAGS, *extra, "-c", str(s), "-o", str(o)],
+                 verbose)
         objs.append(o)
     lib = lib_path()
     if force or _stale(lib, objs):
-        _run([NVCC, *ARCH_FLAGS, "-shared", "-Xlinker", f"-soname={LIB_NAME}", "-o", str(lib),
+        _run([NVCC, "-ccbin", host_cxx(), *ARCH_FLAGS, "-shared", "-Xlinker", f"-soname={LIB_NAME}", "-o", str(lib),
               *map(str, objs)], verbose)
     return lib
 
@@ -90,7 +104,7 @@ def build_ext(force: bool = False, verbose: bool = False) -> Path:
     deps = [src, INCLUDE / "fa_sm100.h", lib_path()]
     if not force and not _stale(out, deps):
         return out
-    cxx = os.environ.get("CXX", shutil.which("g++") or "g++")
+    cxx = host_cxx()
     abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
     incs = [*cpp_extension.include_paths(), sysconfig.get_paths()["include"], str(CUDA_HOME / "include"),
             str(INCLUDE)]

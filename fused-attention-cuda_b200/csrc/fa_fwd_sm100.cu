@@ -338,8 +338,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int row = q0 + r;
     const uint32_t tl = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const float sl2 = args.scale_log2;
+    constexpr bool kRoundedNorm = std::is_same<T, __nv_bfloat16>::value;
     float m_ref = -INFINITY;  // max used in the exponents (raw score units)
-    float l_sum = 0.f;
+    float l_sum = 0.f;        // running sum of the fp32 weights (-> lse)
+    float lq_sum = 0.f;       // running sum of the rounded weights (bf16: -> 1/l of O)
     bool ok = true;
     for (int j = 0; j < n_tiles; ++j) {
       ok = __all_sync(0xffffffffu, wait_bounded(bar(L::kBarSFull + (j & 1)),
@@ -373,20 +375,28 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float alpha =
           resc ? ((m_ref == -INFINITY) ? 0.f : ex2_approx((m_ref - m_use) * sl2)) : 1.f;
       const float mc = (m_use == -INFINITY) ? 0.f : m_use * sl2;
-      float rs = 0.f;
+      float rs = 0.f;   // sum of the fp32 weights: the logsumexp uses this one
+      float rsq = 0.f;  // bf16 only: sum of the rounded weights, the normaliser of O
       uint32_t pk[BN / 2];
 #pragma unroll
       for (int c = 0; c < BN / 2; ++c) {
         const float p0 = ex2_approx(fmaf(s[2 * c], sl2, -mc));
         const float p1 = ex2_approx(fmaf(s[2 * c + 1], sl2, -mc));
-        rs += p0 + p1;
         pk[c] = pack2<T>(p0, p1);
+        rs += p0 + p1;
+        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+          // bf16 keeps 8 significant bits: O is normalised by the sum of the ROUNDED weights
+          // the tensor core multiplies, so o stays a convex combination of V rows and the
+          // common-mode part of the rounding error cancels (rows with few keys).
+          rsq += __uint_as_float(pk[c] << 16) + __uint_as_float(pk[c] & 0xFFFF0000u);
+        }
       }
       const uint32_t pcol = (j & 1) ? L::kColP1 : L::kColP0;
 #pragma unroll
       for (int c = 0; c < BN / 2; c += 16) tmem_st16(tl + pcol + c, &pk[c]);
       tmem_st_wait();
       l_sum = l_sum * alpha + rs;
+      if constexpr (kRoundedNorm) lq_sum = lq_sum * alpha + rsq;
       m_ref = m_use;
       if (j > 0) {
         // PV_{j-1} must be complete before O may be touched (and, for phase bookkeeping, it is
@@ -417,7 +427,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (ok) {
       tc_fence_after();
-      const float inv_l = (l_sum > 0.f) ? 1.f / l_sum : 0.f;
+      const float l_norm = kRoundedNorm ? lq_sum : l_sum;
+      const float inv_l = (l_norm > 0.f) ? 1.f / l_norm : 0.f;
       const bool in_range = row < args.N;
       T* orow = reinterpret_cast<T*>(args.o) +
                 (static_cast<size_t>(bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)) * D;

@@ -1,0 +1,53 @@
+"""Failure detection on the GPU without a GPU fault (marker ``gpu``).
+
+Every mbarrier wait in the kernel is bounded.  Here a wait is made to run out on purpose by a
+host-side injection: the producer warp skips the K load of one key tile, so the MMA warp's wait
+for it can never complete.  With a 100 ms limit the kernel must record the cause
+(kStKFull), drain its own copies and MMAs, free its tensor memory and exit normally; the host
+reads cudaErrorLaunchTimeout from fa_last_device_error(), and the very next launch on the same
+context runs correctly.  No trap, no device assert, no bad address, no endless loop.
+"""
+
+from __future__ import annotations
+
+import pytest
+import torch
+
+import fused_attn
+import oracle
+
+pytestmark = pytest.mark.gpu
+
+K_FULL_BIT = 1 << 1
+LAUNCH_TIMEOUT = 702
+
+
+@pytest.fixture
+def restore_knobs():
+    yield
+    if fused_attn.is_available():
+        fused_attn.debug_set_skip_kv_tile(-1)
+        fused_attn.set_wait_timeout_ns(2_000_000_000)
+
+
+def test_bounded_wait_runs_out_and_context_survives(make_qkv, restore_knobs):
+    if not fused_attn.is_available() or not fused_attn.impl_supports(5, torch.float16, 64):
+        pytest.skip("kernel not available")
+    q, k, v = make_qkv(1, 2, 512, 64, dtype=torch.float16, device="cuda", seed=41)
+    assert fused_attn.last_device_error() == (0, 0)
+
+    fused_attn.set_wait_timeout_ns(100_000_000)
+    fused_attn.debug_set_skip_kv_tile(1)
+    fused_attn.forward(q, k, v, is_causal=False)
+    err, bits = fused_attn.last_device_error()  # synchronises: the launch has ended
+    assert err == LAUNCH_TIMEOUT
+    assert bits & K_FULL_BIT, f"cause bits {bits:#x}"
+    assert fused_attn.last_device_error() == (0, 0)  # read-and-clear
+
+    fused_attn.debug_set_skip_kv_tile(-1)
+    fused_attn.set_wait_timeout_ns(2_000_000_000)
+    o, lse = fused_attn.forward(q, k, v, is_causal=False, return_lse=True)
+    torch.cuda.synchronize()
+    assert fused_attn.last_device_error() == (0, 0)
+    o_ref, lse_ref = oracle.attention(q, k, v, threads=oracle.default_threads())
+    assert oracle.max_abs(o, o_ref) <= 2e-3 and oracle.max_abs(lse, lse_ref) <= 1e-3

@@ -1,0 +1,368 @@
+"""GPU parity of the sm_100a kernel against the CPU oracle (marker ``gpu``).
+
+Reference counterpart: tests/test_kernels_gpu.py.  Gate, per output element, against the fp64
+oracle run on the very (rounded) inputs the kernel saw:
+
+    fp16: max|O - O_ref| <= 2e-3 and max|LSE - LSE_ref| <= 1e-3
+    bf16: max|O - O_ref| <= 8e-3 and max|LSE - LSE_ref| <= 1e-3
+
+plus the reference's secondary FlashAttention ratio rule (error <= 2x PyTorch's own unfused
+attention in the same dtype + 1e-6) and its absolute caps.  Configs too large for the oracle in
+seconds (N >= 4096) are checked on sampled rows (first, middle and last query tiles of the first
+and last heads, as the reference's fa_bench self-check does) and, over the whole tensor, against
+PyTorch's fp32 SDPA on the GPU.
+"""
+
+from __future__ import annotations
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import fused_attn
+import oracle
+from conftest import GOLDEN_DIR
+from fused_attn import abi
+from fused_attn.workloads import C3_SWEEP_N, CONFIGS
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = [torch.float16, torch.bfloat16]
+TOL_O = {torch.float16: 2e-3, torch.bfloat16: 8e-3}
+TOL_LSE = {torch.float16: 1e-3, torch.bfloat16: 1e-3}
+ABS_CAP = {torch.float16: 1e-2, torch.bfloat16: 5e-2}
+_ids = {torch.float16: "fp16", torch.bfloat16: "bf16", torch.float32: "fp32"}
+THREADS = oracle.default_threads()
+
+
+def dtype_id(dt):
+    return _ids[dt]
+
+
+def require(dtype=torch.float16, d=64):
+    if not fused_attn.is_available():
+        pytest.skip("fused_attn._C is not built")
+    if not fused_attn.impl_supports(5, dtype, d):
+        cap = torch.cuda.get_device_capability()
+        pytest.skip(f"not built for {_ids[dtype]} D={d} on sm_{cap[0]}{cap[1]}")
+
+
+@pytest.fixture
+def reset_overrides():
+    yield
+    if fused_attn.is_available():
+        fused_attn.set_debug_overrides(0, 0)
+
+
+def unfused_same_dtype(q, k, v, causal, scale=None):
+    """PyTorch's naive attention in the input dtype (reference.py:288-311): the ratio term."""
+    h, hkv = q.shape[1], k.shape[1]
+    if h != hkv:
+        k = k.repeat_interleave(h // hkv, dim=1)
+        v = v.repeat_interleave(h // hkv, dim=1)
+    scale = 1.0 / math.sqrt(q.shape[-1]) if scale is None else scale
+    s = torch.matmul(q * scale, k.transpose(-1, -2))
+    if causal:
+        n = q.shape[2]
+        s = s.masked_fill(~torch.ones(n, n, dtype=torch.bool, device=q.device).tril(), float("-inf"))
+    return torch.matmul(torch.softmax(s, dim=-1), v)
+
+
+def check(o, lse, q, k, v, causal, dtype, scale=None, ratio=True):
+    """Full-tensor gate against the oracle.  Returns (err_o, err_lse)."""
+    assert o.shape == q.shape and o.dtype == dtype and o.is_contiguous()
+    assert lse.shape == q.shape[:3] and lse.dtype == torch.float32
+    assert bool(torch.isfinite(o).all()), "kernel produced NaN/inf"
+    assert bool(torch.isfinite(lse).all())
+    o_ref, lse_ref = oracle.attention(q, k, v, causal=causal, scale=scale, threads=THREADS)
+    eo = oracle.max_abs(o, o_ref)
+    el = oracle.max_abs(lse, lse_ref)
+    assert eo <= TOL_O[dtype], f"max|O - O_ref| = {eo:.3e} > {TOL_O[dtype]}"
+    assert el <= TOL_LSE[dtype], f"max|LSE - LSE_ref| = {el:.3e} > {TOL_LSE[dtype]}"
+    if ratio:
+        r = oracle.error_ratio(o, o_ref, unfused_same_dtype(q, k, v, causal, scale))
+        assert r.ok, f"ratio rule failed: {r}"
+        assert r.err_mine <= ABS_CAP[dtype]
+    return eo, el
+
+
+def check_rows(o, lse, q, k, v, causal, dtype, row_blocks, scale=None):
+    """Oracle on selected (b, h, row0, nrows) blocks only (large configs)."""
+    o_c, lse_c = o.float().cpu(), lse.cpu()
+    qc, kc, vc = q.cpu(), k.cpu(), v.cpu()
+    for b, h, r0, nr in row_blocks:
+        o_ref, lse_ref = oracle.rows(qc, kc, vc, b, h, r0, nr, causal=causal, scale=scale)
+        eo = oracle.max_abs(o_c[b, h, r0:r0 + nr], o_ref)
+        el = oracle.max_abs(lse_c[b, h, r0:r0 + nr], lse_ref)
+        assert eo <= TOL_O[dtype], f"rows {(b, h, r0, nr)}: max|dO| = {eo:.3e}"
+        assert el <= TOL_LSE[dtype], f"rows {(b, h, r0, nr)}: max|dLSE| = {el:.3e}"
+
+
+def check_vs_sdpa_fp32(o, q, k, v, causal, dtype):
+    """Whole-tensor comparison against PyTorch fp32 SDPA (a floating-point reference of the
+    same op, on the same rounded inputs), for configs too large for the oracle."""
+    import torch.nn.functional as F
+
+    h, hkv = q.shape[1], k.shape[1]
+    ref = F.scaled_dot_product_attention(q.float(), k.float(), v.float(), is_causal=causal,
+                                         enable_gqa=h != hkv)
+    err = float((o.float() - ref).abs().max())
+    assert err <= TOL_O[dtype], f"max|O - SDPA_fp32| = {err:.3e}"
+
+
+def sample_blocks(b, h, n, tile=128):
+    mid = (n // 2 // tile) * tile
+    starts = sorted({0, mid, max(0, n - tile)})
+    return [(bb, hh, r0, min(tile, n - r0)) for bb, hh in {(0, 0), (b - 1, h - 1)} for r0 in starts]
+
+
+# ------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+@pytest.mark.parametrize("dtype", DTYPES, ids=dtype_id)
+def test_matches_oracle(dtype, causal, gpu_shape, make_qkv):
+    b, h, n, d = gpu_shape
+    require(dtype, d)
+    q, k, v = make_qkv(b, h, n, d, dtype=dtype, device="cuda")
+    o, lse = fused_attn.forward_stage(q, k, v, 5, is_causal=causal)
+    check(o, lse, q, k, v, causal, dtype)
+
+
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("n", [32, 96, 160, 224, 416])
+def test_ragged_sequence_lengths(n, d, causal, make_qkv):
+    """N % 32 == 0 but not a multiple of the 128-row tile: partial query and key tiles."""
+    require(torch.float16, d)
+    q, k, v = make_qkv(2, 3, n, d, dtype=torch.float16, device="cuda", seed=21)
+    o, lse = fused_attn.forward(q, k, v, is_causal=causal, return_lse=True)
+    check(o, lse, q, k, v, causal, torch.float16)
+
+
+@pytest.mark.parametrize("name", ["C2", "C2c", "C3", "C3bf16"])
+def test_baseline_configs(name, make_qkv):
+    cfg = CONFIGS[name]
+    require(cfg.dtype, cfg.D)
+    q, k, v = make_qkv(cfg.B, cfg.H, cfg.N, cfg.D, dtype=cfg.dtype, device="cuda", seed=cfg.seed)
+    o, lse = fused_attn.forward(q, k, v, is_causal=cfg.causal, return_lse=True)
+    check(o, lse, q, k, v, cfg.causal, cfg.dtype, ratio=False)
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=dtype_id)
+@pytest.mark.parametrize("n", C3_SWEEP_N)
+def test_c3_sequence_sweep(n, dtype, make_qkv):
+    require(dtype, 128)
+    q, k, v = make_qkv(2, 8, n, 128, dtype=dtype, device="cuda", seed=2)
+    o, lse = fused_attn.forward(q, k, v, is_causal=True, return_lse=True)
+    if n <= 1024:
+        check(o, lse, q, k, v, True, dtype, ratio=False)
+    else:
+        check_rows(o, lse, q, k, v, True, dtype, sample_blocks(2, 8, n))
+        check_vs_sdpa_fp32(o, q, k, v, True, dtype)
+
+
+def test_c4_long_context_rows(make_qkv):
+    """C4 (B1 H32 N16384 D128 bf16 causal, seed 3) on one GPU: sampled rows vs the oracle and
+    the whole tensor vs fp32 SDPA."""
+    cfg = CONFIGS["C4"]
+    require(cfg.dtype, cfg.D)
+    q, k, v = make_qkv(cfg.B, cfg.H, cfg.N, cfg.D, dtype=cfg.dtype, device="cuda", seed=cfg.seed)
+    o, lse = fused_attn.forward(q, k, v, is_causal=True, return_lse=True)
+    assert bool(torch.isfinite(o).all()) and bool(torch.isfinite(lse).all())
+    blocks = [(0, 0, 0, 64), (0, 0, cfg.N - 64, 64), (0, 31, cfg.N // 2, 64), (0, 17, cfg.N - 32, 32)]
+    check_rows(o, lse, q, k, v, True, cfg.dtype, blocks)
+    check_vs_sdpa_fp32(o, q, k, v, True, cfg.dtype)
+
+
+# ------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("dtype", DTYPES, ids=dtype_id)
+@pytest.mark.parametrize("name", ["fp16_n64", "bf16_n96_d128", "fp16_scale005_d128"])
+def test_golden_fixtures(name, dtype):
+    """The kernel against outputs the reference's own oracles produced (tests/golden)."""
+    g = np.load(GOLDEN_DIR / "golden.npz")
+    b, h, hkv, n, d, seed, dt = (int(x) for x in g[f"{name}/meta"])
+    want_dtype = {1: torch.float16, 2: torch.bfloat16}.get(dt)
+    if want_dtype != dtype:
+        pytest.skip("fixture stored for the other dtype")
+    require(dtype, d)
+    scale = float(g[f"{name}/scale"][0])
+    scale = None if math.isnan(scale) else scale
+    q, k, v = (torch.from_numpy(g[f"{name}/{t}"].astype(np.float32)).to("cuda", dtype) for t in "qkv")
+    for causal in (False, True):
+        tag = "causal" if causal else "full"
+        o, lse = fused_attn.forward(q, k, v, is_causal=causal, scale=scale, return_lse=True)
+        eo = oracle.max_abs(o, g[f"{name}/{tag}/o"])
+        el = oracle.max_abs(lse, g[f"{name}/{tag}/lse"])
+        assert eo <= TOL_O[dtype] and el <= TOL_LSE[dtype], (tag, eo, el)
+
+
+# ------------------------------------------------------------------------------------------
+def test_forward_dispatches_to_stage5(make_qkv):
+    require()
+    q, k, v = make_qkv(1, 2, 256, 64, dtype=torch.float16, device="cuda")
+    o, lse = fused_attn.forward(q, k, v, is_causal=True, return_lse=True)
+    o5, lse5 = fused_attn.forward_stage(q, k, v, 5, is_causal=True)
+    assert torch.equal(o, o5) and torch.equal(lse, lse5)
+
+
+@pytest.mark.parametrize("n", [128, 256])
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+@pytest.mark.parametrize("dtype", DTYPES, ids=dtype_id)
+def test_tile_invariance(dtype, causal, n, make_qkv, reset_overrides):
+    """The online-softmax rescale only runs when a row spans several key tiles: the same
+    problem with block_n in {128, 64, 32} must pass the gate every time and agree."""
+    require(dtype, 64)
+    q, k, v = make_qkv(2, 2, n, 64, dtype=dtype, device="cuda", seed=11)
+    outs = {}
+    for bm, bn in [(0, 0), (0, 64), (0, 32), (128, 32)]:
+        fused_attn.set_debug_overrides(bm, bn)
+        o, lse = fused_attn.forward_stage(q, k, v, 5, is_causal=causal)
+        torch.cuda.synchronize()
+        check(o, lse, q, k, v, causal, dtype)
+        outs[(bm, bn)] = o.double()
+    fused_attn.set_debug_overrides(0, 0)
+    base = outs[(0, 0)]
+    for key, o in outs.items():
+        assert float((o - base).abs().max()) <= 2 * TOL_O[dtype], key
+
+
+def test_unbuilt_tile_override_is_rejected(make_qkv, reset_overrides):
+    require()
+    q, k, v = make_qkv(1, 1, 128, 64, dtype=torch.float16, device="cuda")
+    for bm, bn in [(64, 0), (0, 48), (0, 256)]:
+        fused_attn.set_debug_overrides(bm, bn)
+        with pytest.raises(RuntimeError, match="invalid argument"):
+            fused_attn.forward(q, k, v)
+    fused_attn.set_debug_overrides(0, 0)
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=dtype_id)
+def test_determinism_50_runs_bitwise_equal(dtype, make_qkv):
+    require(dtype, 64)
+    q, k, v = make_qkv(2, 4, 256, 64, dtype=dtype, device="cuda", seed=12)
+    first, first_lse = fused_attn.forward_stage(q, k, v, 5, is_causal=True)
+    for _ in range(49):
+        o, lse = fused_attn.forward_stage(q, k, v, 5, is_causal=True)
+        assert torch.equal(o, first) and torch.equal(lse, first_lse)
+
+
+@pytest.mark.parametrize("factor", [1e2, 1e-3], ids=["x1e2", "x1e-3"])
+@pytest.mark.parametrize("dtype", DTYPES, ids=dtype_id)
+def test_half_precision_dynamic_range(dtype, factor, make_qkv):
+    """Scores past fp16's range must stay in fp32 (x1e2); tiny scores (x1e-3)."""
+    require(dtype, 64)
+    q, k, v = make_qkv(1, 2, 256, 64, dtype=dtype, device="cuda", seed=13, scale_inputs=factor)
+    o, lse = fused_attn.forward_stage(q, k, v, 5)
+    assert bool(torch.isfinite(o).all()) and bool(torch.isfinite(lse).all())
+    o_ref, lse_ref = oracle.attention(q, k, v, threads=THREADS)
+    rel = oracle.max_abs(o, o_ref) / max(float(np.abs(o_ref).max()), 1e-30)
+    assert rel <= ABS_CAP[dtype]
+    assert oracle.max_abs(lse, lse_ref) <= max(TOL_LSE[dtype], 1e-6 * float(np.abs(lse_ref).max()))
+
+
+@pytest.mark.parametrize("dtype", DTYPES, ids=dtype_id)
+def test_causal_equals_explicit_tril_mask(dtype, make_qkv):
+    require(dtype, 64)
+    n = 512
+    q, k, v = make_qkv(1, 2, n, 64, dtype=dtype, device="cuda", seed=14)
+    o, _ = fused_attn.forward_stage(q, k, v, 5, is_causal=True)
+    o_mask, _ = oracle.numpy_attention(q, k, v, keep=np.tril(np.ones((n, n), dtype=bool)))
+    assert oracle.max_abs(o, o_mask) <= TOL_O[dtype]
+    # query 0 sees key 0 only: o[0] == v[0] exactly (v[0] is representable in the dtype)
+    assert torch.equal(o[:, :, 0, :], v[:, :, 0, :])
+
+
+@pytest.mark.parametrize("scale", [0.05, 0.25])
+@pytest.mark.parametrize("dtype", DTYPES, ids=dtype_id)
+def test_non_default_scale(dtype, scale, make_qkv):
+    require(dtype, 128)
+    q, k, v = make_qkv(1, 2, 256, 128, dtype=dtype, device="cuda", seed=15)
+    o, lse = fused_attn.forward_stage(q, k, v, 5, is_causal=False, scale=scale)
+    check(o, lse, q, k, v, False, dtype, scale=scale)
+
+
+@pytest.mark.parametrize("h,hkv", [(4, 2), (8, 1), (6, 3)])
+@pytest.mark.parametrize("dtype", DTYPES, ids=dtype_id)
+def test_gqa_heads(dtype, h, hkv, make_qkv):
+    require(dtype, 64)
+    q, k, v = make_qkv(2, h, 256, 64, dtype=dtype, device="cuda", hkv=hkv, seed=17)
+    o, lse = fused_attn.forward_stage(q, k, v, 5, is_causal=True)
+    check(o, lse, q, k, v, True, dtype)
+
+
+# ------------------------------------------------------------------------------------------
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+def test_c_abi_direct_call_equals_op_and_overwrites_poison(causal, make_qkv):
+    """fa_forward through ctypes on caller-owned, NaN-poisoned buffers on torch's current
+    stream: every O/LSE element is written and equals the op's result bit for bit."""
+    require()
+    b, h, n, d = 2, 3, 352, 128
+    q, k, v = make_qkv(b, h, n, d, dtype=torch.float16, device="cuda", seed=31)
+    o = torch.full_like(q, float("nan"))
+    lse = torch.full((b, h, n), float("nan"), device="cuda", dtype=torch.float32)
+    p = abi.params(b, h, h, n, d, 1.0 / math.sqrt(d), causal)
+    stream = torch.cuda.current_stream().cuda_stream
+    err = abi.forward(abi.FA_IMPL_TUNED, abi.FA_DTYPE_F16, q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                      o.data_ptr(), lse.data_ptr(), p, stream)
+    assert err == 0
+    torch.cuda.synchronize()
+    assert bool(torch.isfinite(o).all()) and bool(torch.isfinite(lse).all())
+    o_op, lse_op = fused_attn.forward(q, k, v, is_causal=causal, return_lse=True)
+    assert torch.equal(o, o_op) and torch.equal(lse, lse_op)
+    assert fused_attn.last_device_error() == (0, 0)
+
+
+def test_c_abi_error_codes_on_device(make_qkv):
+    require()
+    q, k, v = make_qkv(1, 2, 128, 64, dtype=torch.float16, device="cuda")
+    o, lse = torch.empty_like(q), torch.empty(1, 2, 128, device="cuda")
+    ptrs = (q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(), lse.data_ptr())
+    p = abi.params(1, 2, 2, 128, 64, 0.125, False)
+    assert abi.forward(abi.FA_IMPL_WMMA, abi.FA_DTYPE_F16, *ptrs, p) == abi.CUDA_ERROR_NOT_SUPPORTED
+    assert abi.forward(abi.FA_IMPL_TUNED, abi.FA_DTYPE_F32, *ptrs, p) == abi.CUDA_ERROR_NOT_SUPPORTED
+    p.N = 100
+    assert abi.forward(abi.FA_IMPL_TUNED, abi.FA_DTYPE_F16, *ptrs, p) == abi.CUDA_ERROR_INVALID_VALUE
+
+
+# ------------------------------------------------------------------------------------------
+def test_n_not_multiple_of_32_raises(make_qkv):
+    require()
+    q, k, v = make_qkv(1, 1, 100, 64, dtype=torch.float16, device="cuda")
+    with pytest.raises(RuntimeError, match="multiple of 32"):
+        fused_attn.forward_stage(q, k, v, 5)
+    with pytest.raises(RuntimeError, match="multiple of 32"):
+        fused_attn.forward(q, k, v)
+
+
+def test_input_validation_messages(make_qkv):
+    require()
+    q, k, v = make_qkv(1, 2, 64, 64, dtype=torch.float16, device="cuda")
+    with pytest.raises((RuntimeError, NotImplementedError)):
+        fused_attn.forward(q.cpu(), k.cpu(), v.cpu())
+    with pytest.raises(RuntimeError, match="contiguous"):
+        fused_attn.forward(q.transpose(1, 2).contiguous().transpose(1, 2), k, v)
+    with pytest.raises(RuntimeError, match="dtype"):
+        fused_attn.forward(q, k.float(), v)
+    with pytest.raises(RuntimeError, match="D must be 64 or 128"):
+        fused_attn.forward(q[..., :32].contiguous(), k[..., :32].contiguous(),
+                           v[..., :32].contiguous())
+    with pytest.raises(RuntimeError, match="stage must be in 1..5"):
+        fused_attn.forward_stage(q, k, v, 0)
+    with pytest.raises(RuntimeError, match="stage must be in 1..5"):
+        fused_attn.forward_stage(q, k, v, 6)
+    with pytest.raises(RuntimeError, match="Nq == Nkv"):
+        fused_attn.forward(q, k[:, :, :32].contiguous(), v[:, :, :32].contiguous())
+    with pytest.raises(RuntimeError, match="multiple of Hkv"):
+        fused_attn.forward(q[:, :1].contiguous(), k, v)
+    with pytest.raises(RuntimeError, match="16-byte aligned"):
+        flat = torch.empty(64 * 64 * 2 + 1, dtype=torch.float16, device="cuda")
+        qm = flat[1:].view(1, 2, 64, 64)
+        fused_attn.forward(qm, k, v)
+    with pytest.raises(RuntimeError, match="scale must be finite"):
+        fused_attn.forward(q, k, v, scale=0.0)
+    for stage in (1, 2, 3, 4):
+        with pytest.raises(RuntimeError, match="not implemented"):
+            fused_attn.forward_stage(q, k, v, stage)
+    with pytest.raises(RuntimeError, match="not implemented|no stage"):
+        fused_attn.forward_stage(q.float(), k.float(), v.float(), 5)
