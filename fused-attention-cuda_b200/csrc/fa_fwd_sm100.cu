@@ -9,25 +9,38 @@
 // Top-left causal: key tiles past the query tile's last row are never loaded
 // (stage5_tuned.cu:532-533); the diagonal tile is masked element-wise (:596-602).
 //
-// One CTA computes one 128-row query tile of one (batch, head).  Warp roles (256 threads):
+// One CTA computes one 128-row query tile of one (batch, head).  Warp roles (384 threads):
 //   warp 0      TMA producer: Q once, then K_j / V_j through a STAGES-deep shared-memory ring
 //               (full/empty mbarrier pairs; K and V have separate slots so K_{j+STAGES} can land
 //               while V_j is still being read).
-//   warp 1      owns tensor memory (alloc/dealloc); lane 0 issues every tcgen05.mma:
-//                 S_j  = Q K_j^T     (SS: both operands in smem, K-major, 128-byte swizzle)
-//                 O   += P_j V_j     (TS: P from TMEM, V from smem as an MN-major operand)
-//               in the order S_0, S_1, PV_0, S_2, PV_1, ... so S_{j+1} runs on the tensor core
-//               while the softmax warps work on S_j.
+//   warp 1      owns tensor memory (alloc/dealloc); lane 0 issues every tcgen05.mma.
 //   warps 2-3   idle (they only join the final barrier).
-//   warps 4-7   softmax warpgroup, one thread per query row (TMEM lane = row): tcgen05.ld of
-//               the S row, masking, row max, exp2, P packed to 16 bit and written back to TMEM
-//               with tcgen05.st, then the O correction when the running max moved.
+//   warps 4-7   softmax warpgroup 0: key tiles j = 0, 2, 4, ...
+//   warps 8-11  softmax warpgroup 1: key tiles j = 1, 3, 5, ...
+// Each softmax warpgroup runs its own online softmax (own running max m_w and sums l_w) over its
+// half of the key tiles into its own accumulator O_w; one thread per query row (TMEM lane = row).
+// The two partial results are merged at the end exactly like two split-KV partials:
+//   m = max(m0, m1), a_w = 2^((m_w - m) c), l = a0 l0 + a1 l1, o = (a0 O0 + a1 O1) / l.
+// Splitting the key tiles (instead of giving each warpgroup its own 128 query rows) keeps the
+// work item at 128 rows, which keeps causal workloads balanced across the 148 SMs.
 //
-// Tensor memory (columns; 128 lanes = 128 query rows): S double buffer [0, 2*BN),
-// O accumulator [2*BN, 2*BN + D), P double buffer of BN/2 columns each after it.  P has its
-// own buffers so the only tensor-core hazards are same-accumulator ones (PV_j after PV_{j-1}),
-// which the hardware orders; everything else is ordered by tcgen05.commit -> mbarrier.
+// Tensor memory (128 lanes = 128 query rows; columns): S_0 [0, BN), S_1 [BN, 2BN),
+// O_0 [2BN, 2BN+D), O_1 [2BN+D, 2BN+2D).  P_w (16-bit, BN/2 columns) is written over the first
+// half of S_w once the S row is in registers, and is the A operand of the TS-MMA O_w += P_w V_j.
+// MMA issue order: S_0(0), S_1(0), then per round t: PV_0(t), S_0(t+1), PV_1(t), S_1(t+1), with
+//   S_w(t)   = Q K_{2t+w}^T          (SS: Q and K in smem, K-major, 128-byte swizzle)
+//   PV_w(t)  : O_w += P_w V_{2t+w}   (TS: P from TMEM, V from smem as an MN-major operand)
+// so the tensor core works for one warpgroup while the other runs its softmax.  S_w(t+1)
+// overwrites the columns PV_w(t) reads right after it; tcgen05.mma instructions issued by one
+// thread execute in issue order, so the reads come first (FlashAttention-4's forward relies on
+// the same order).  The commit of S_w(t+1) covers every earlier MMA, so a softmax warpgroup that
+// sees S_w(t+1) complete also knows PV_w(t) is complete before it rescales O_w.
 //
+// bf16 keeps 8 significant bits.  Rows of the first causal query tile average only a handful of
+// keys, where rounding P to bf16 would add up to ~2^-9 |v| to the output's own rounding; there P
+// is carried as P_hi + P_lo (both bf16, the second half of S_w holds P_lo) and multiplied twice.
+// Every other row averages >= 128 keys and its rounding errors average out.
+
 // O rescaling is lazy: the max used for the exponent (m_ref) only moves when the tile max
 // exceeds it by more than 2^8 in exponent units, so P stays <= 256 (exact in fp16/bf16 range)
 // and the O read-modify-write through TMEM is rare.  The final o = acc/l and lse use the same
@@ -36,6 +49,7 @@
 // Every mbarrier wait is bounded (globaltimer); a wait that runs out sets a CTA-local abort flag,
 // records a cause bit in g_status and the launch epoch in g_abort_epoch (so other CTAs of the
 // same launch stop early), then the CTA drains its own TMA copies and MMAs, frees TMEM and exits.
+// Named barriers are always reached by all of their threads, on the abort path too.
 #include <climits>
 #include <cmath>
 #include <cstdio>
@@ -56,8 +70,9 @@ __device__ unsigned int g_abort_epoch;  // epoch of the last launch in which a w
 namespace {
 
 constexpr int kBlockM = 128;
-constexpr int kThreads = 256;
-constexpr int kSoftmaxThread0 = 128;  // warps 4..7
+constexpr int kThreads = 384;
+constexpr int kSoftmaxWarp0 = 4;  // warps 4..11: two softmax warpgroups
+constexpr int kMergeBarrier = 1;  // named barrier id shared by the 256 softmax threads
 constexpr float kRescaleThreshold = 8.0f;
 
 template <int D, int BN, int STAGES>
@@ -73,17 +88,15 @@ struct Layout {
   static constexpr int kKOff = kQOff + kQBytes;
   static constexpr int kVOff = kKOff + STAGES * kKVBytes;
   static constexpr int kBarOff = kVOff + STAGES * kKVBytes;
-  static constexpr int kNumBars = 7 + 4 * STAGES;
+  static constexpr int kNumBars = 8 + 4 * STAGES;
   static constexpr int kMiscOff = kBarOff + 8 * kNumBars;
   static constexpr int kBytes = kMiscOff + 16;
   static constexpr int kSmemAlloc = kBytes + 1024;  // slack to align the base to 1024 bytes
 
-  static constexpr int kColS0 = 0;
-  static constexpr int kColS1 = BN;
-  static constexpr int kColO = 2 * BN;
-  static constexpr int kColP0 = 2 * BN + D;
-  static constexpr int kColP1 = 2 * BN + D + BN / 2;
-  static constexpr int kColsUsed = 3 * BN + D;
+  // Tensor memory columns.
+  static constexpr int kColS = 0;       // + w * BN
+  static constexpr int kColO = 2 * BN;  // + w * D
+  static constexpr int kColsUsed = 2 * BN + 2 * D;
   static constexpr int kTmemCols = kColsUsed <= 32    ? 32
                                    : kColsUsed <= 64  ? 64
                                    : kColsUsed <= 128 ? 128
@@ -92,15 +105,18 @@ struct Layout {
 
   // Barrier indices.
   static constexpr int kBarQ = 0;
-  static constexpr int kBarKFull = 1;                 // + stage
-  static constexpr int kBarVFull = 1 + STAGES;        // + stage
-  static constexpr int kBarKEmpty = 1 + 2 * STAGES;   // + stage
-  static constexpr int kBarVEmpty = 1 + 3 * STAGES;   // + stage
-  static constexpr int kBarSFull = 1 + 4 * STAGES;    // + buffer
-  static constexpr int kBarPFull = 3 + 4 * STAGES;    // + buffer
-  static constexpr int kBarODone = 5 + 4 * STAGES;
-  static constexpr int kBarDrain = 6 + 4 * STAGES;
+  static constexpr int kBarKFull = 1;                // + stage
+  static constexpr int kBarVFull = 1 + STAGES;       // + stage
+  static constexpr int kBarKEmpty = 1 + 2 * STAGES;  // + stage
+  static constexpr int kBarVEmpty = 1 + 3 * STAGES;  // + stage
+  static constexpr int kBarSFull = 1 + 4 * STAGES;   // + warpgroup
+  static constexpr int kBarPFull = 3 + 4 * STAGES;   // + warpgroup
+  static constexpr int kBarPVDone = 5 + 4 * STAGES;  // + warpgroup
+  static constexpr int kBarDrain = 7 + 4 * STAGES;
 
+  // The merge exchange (m, l per row and warpgroup) reuses the Q tile once every MMA is done.
+  static constexpr int kMergeFloats = 2 * 2 * kBlockM;
+  static_assert(kMergeFloats * 4 <= kQBytes, "merge exchange must fit in the Q tile");
   static_assert(D % kSwElems == 0, "D must be a multiple of the swizzle width");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 128, "BN must be 32, 64 or 128");
   static_assert(kColsUsed <= 512, "tensor memory overflow");
@@ -164,6 +180,87 @@ __device__ __forceinline__ void wait_drain(uint32_t bar, uint32_t parity,
   }
 }
 
+// Every kEmuEvery-th pair of exponentials goes to the FMA pipes (ex2_poly3) instead of the MUFU
+// unit; 0 keeps them all on MUFU.  Set at build time with -DFA_EX2_EMU_EVERY=n.
+#ifndef FA_EX2_EMU_EVERY
+#define FA_EX2_EMU_EVERY 0
+#endif
+constexpr int kEmuEvery = FA_EX2_EMU_EVERY;
+
+// Loads one S row (BN fp32 columns of this thread's TMEM lane) with one instruction.
+template <int BN>
+__device__ __forceinline__ void load_s_row(uint32_t taddr, float (&s)[BN]) {
+  uint32_t u[BN];
+  if constexpr (BN == 128) {
+    tmem_ld128_wait(taddr, u);
+  } else if constexpr (BN == 64) {
+    tmem_ld64_wait(taddr, u);
+  } else {
+    tmem_ld32_wait(taddr, u);
+  }
+#pragma unroll
+  for (int i = 0; i < BN; ++i) s[i] = __uint_as_float(u[i]);
+}
+
+// Row maximum with four independent three-input max chains (BN/8 deep instead of BN).
+template <int BN>
+__device__ __forceinline__ float row_max(const float (&s)[BN]) {
+  float a0 = fmaxf(s[0], s[1]), a1 = fmaxf(s[2], s[3]);
+  float a2 = fmaxf(s[4], s[5]), a3 = fmaxf(s[6], s[7]);
+#pragma unroll
+  for (int i = 8; i < BN; i += 8) {
+    a0 = fmax3(a0, s[i + 0], s[i + 1]);
+    a1 = fmax3(a1, s[i + 2], s[i + 3]);
+    a2 = fmax3(a2, s[i + 4], s[i + 5]);
+    a3 = fmax3(a3, s[i + 6], s[i + 7]);
+  }
+  return fmax3(fmaxf(a0, a1), a2, a3);
+}
+
+// p = 2^(s*c - m*c) for one S row: the exponent argument in packed fp32 pairs, the exponential
+// on MUFU (and every kEmuEvery-th pair on the FMA pipes), P packed two per 32-bit word and stored
+// to TMEM at `taddr` (BN/2 columns).  Returns the row sum of the fp32 weights, accumulated in
+// four packed partial sums.  kLo (bf16 only) also stores P_lo = p - bf16(p) in the next BN/2
+// columns.
+template <typename T, int BN, bool kLo>
+__device__ __forceinline__ float exp_pack_store(const float (&s)[BN], float sl2, float mc,
+                                                uint32_t taddr) {
+  const uint64_t c2 = f2_pack(sl2, sl2);
+  const uint64_t nb2 = f2_pack(-mc, -mc);
+  uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+  uint32_t pk[BN / 2];
+  uint32_t lo[kLo ? BN / 2 : 1];
+#pragma unroll
+  for (int c = 0; c < BN / 2; ++c) {
+    const uint64_t x = f2_fma(f2_pack(s[2 * c], s[2 * c + 1]), c2, nb2);
+    float p0, p1;
+    if (kEmuEvery > 0 && (c % (kEmuEvery > 0 ? kEmuEvery : 1)) == (kEmuEvery > 0 ? kEmuEvery : 1) - 1) {
+      p0 = ex2_poly3(f2_lo(x));
+      p1 = ex2_poly3(f2_hi(x));
+    } else {
+      p0 = ex2_approx(f2_lo(x));
+      p1 = ex2_approx(f2_hi(x));
+    }
+    pk[c] = pack2<T>(p0, p1);
+    acc[c & 3] = f2_add(acc[c & 3], f2_pack(p0, p1));
+    if constexpr (kLo) {
+      lo[c] = pack2<T>(p0 - __uint_as_float(pk[c] << 16), p1 - __uint_as_float(pk[c] & 0xFFFF0000u));
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < BN / 2; c += 16) tmem_st16(taddr + c, &pk[c]);
+  if constexpr (kLo) {
+#pragma unroll
+    for (int c = 0; c < BN / 2; c += 16) tmem_st16(taddr + BN / 2 + c, &lo[c]);
+  }
+  const uint64_t t = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
+  return f2_lo(t) + f2_hi(t);
+}
+
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 template <typename T, int D, int BN, int STAGES, bool CAUSAL>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -200,7 +297,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int h_idx = bh - b_idx * args.H;
   const int bh_kv = b_idx * args.Hkv + h_idx / (args.H / args.Hkv);
   const int kv_end = CAUSAL ? min(args.N, q0 + kBlockM) : args.N;
-  const int n_tiles = (kv_end + BN - 1) / BN;
+  const int n_tiles = (kv_end + BN - 1) / BN;  // >= 1
+  const int n_t0 = (n_tiles + 1) / 2;          // tiles of warpgroup 0 (even j)
+  const int n_t1 = n_tiles / 2;                // tiles of warpgroup 1 (odd j)
+  // bf16 keeps 8 significant bits.  In the first causal query tile the rows average only a
+  // handful of keys, so rounding P to bf16 would add up to ~2^-9 |v| on top of the output
+  // rounding; there P is carried as P_hi + P_lo (two bf16 MMAs).  Everywhere else a row averages
+  // >= 128 keys and the rounding errors average out.
+  const bool comp = std::is_same<T, __nv_bfloat16>::value && CAUSAL && q_tile == 0;
 
   if (threadIdx.x == 0) {
     mbar_init(bar(L::kBarQ), 1);
@@ -210,11 +314,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(bar(L::kBarKEmpty + s), 1);
       mbar_init(bar(L::kBarVEmpty + s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(bar(L::kBarSFull + b), 1);
-      mbar_init(bar(L::kBarPFull + b), kBlockM);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(bar(L::kBarSFull + g), 1);
+      mbar_init(bar(L::kBarPFull + g), kBlockM);
+      mbar_init(bar(L::kBarPVDone + g), 1);
     }
-    mbar_init(bar(L::kBarODone), 1);
     mbar_init(bar(L::kBarDrain), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -282,15 +386,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t kIdescS = idesc_mma(kFmt, kBlockM, BN, false);
       constexpr uint32_t kIdescPV = idesc_mma(kFmt, kBlockM, D, true);
-      bool ok = wait_bounded(bar(L::kBarQ), 0u, w, kStQFull);
-      auto issue_s = [&](int j) -> bool {
+      // S_g(t) = Q K_j^T, j = 2t + g, into S_g.
+      auto issue_s = [&](int g, int t) -> bool {
+        const int j = 2 * t + g;
         const int s = j % STAGES;
         if (!wait_bounded(bar(L::kBarKFull + s), static_cast<uint32_t>(j / STAGES) & 1u, w,
                           kStKFull)) {
           return false;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem + ((j & 1) ? L::kColS1 : L::kColS0);
+        const uint32_t d_tmem = tmem + L::kColS + g * BN;
         const uint32_t kb = sbase + L::kKOff + s * L::kKVBytes;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
@@ -299,64 +404,85 @@ __global__ void __launch_bounds__(kThreads, 1)
           umma_ss(d_tmem, sdesc_sw128(sbase + L::kQOff + q_off, 16, 1024),
                   sdesc_sw128(kb + k_off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
         }
-        umma_commit(bar(L::kBarSFull + (j & 1)));
+        umma_commit(bar(L::kBarSFull + g));
         umma_commit(bar(L::kBarKEmpty + s));
         return true;
       };
-      if (ok) ok = issue_s(0);
-      for (int j = 0; ok && j < n_tiles; ++j) {
-        if (j + 1 < n_tiles) {
-          ok = issue_s(j + 1);
-          if (!ok) break;
-        }
-        ok = wait_bounded(bar(L::kBarPFull + (j & 1)), static_cast<uint32_t>(j >> 1) & 1u, w,
-                          kStPFull);
-        if (!ok) break;
+      // O_g += P_g V_j, j = 2t + g.  With `comp` (bf16 causal query tile 0) P_g is two bf16
+      // halves P_hi + P_lo in the two halves of S_g, and both are multiplied.
+      auto issue_pv = [&](int g, int t, bool last) -> bool {
+        const int j = 2 * t + g;
         const int s = j % STAGES;
-        ok = wait_bounded(bar(L::kBarVFull + s), static_cast<uint32_t>(j / STAGES) & 1u, w,
-                          kStVFull);
-        if (!ok) break;
+        if (!wait_bounded(bar(L::kBarPFull + g), static_cast<uint32_t>(t) & 1u, w, kStPFull)) {
+          return false;
+        }
+        if (!wait_bounded(bar(L::kBarVFull + s), static_cast<uint32_t>(j / STAGES) & 1u, w,
+                          kStVFull)) {
+          return false;
+        }
         tc_fence_after();
         const uint32_t vb = sbase + L::kVOff + s * L::kKVBytes;
-        const uint32_t pa = tmem + ((j & 1) ? L::kColP1 : L::kColP0);
+        const uint32_t pa = tmem + L::kColS + g * BN;
+        const uint32_t o_tmem = tmem + L::kColO + g * D;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          umma_ts(tmem + L::kColO, pa + kk * 8, sdesc_sw128(vb + kk * 16 * 128, L::kKVChunkBytes, 1024),
-                  kIdescPV, (j > 0 || kk > 0) ? 1u : 0u);
+          umma_ts(o_tmem, pa + kk * 8, sdesc_sw128(vb + kk * 16 * 128, L::kKVChunkBytes, 1024),
+                  kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
         }
-        umma_commit(bar(L::kBarODone));
+        if (comp) {
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            umma_ts(o_tmem, pa + BN / 2 + kk * 8,
+                    sdesc_sw128(vb + kk * 16 * 128, L::kKVChunkBytes, 1024), kIdescPV, 1u);
+          }
+        }
+        if (last) umma_commit(bar(L::kBarPVDone + g));
         umma_commit(bar(L::kBarVEmpty + s));
+        return true;
+      };
+      // Issue order PV_0(t), S_0(t+1), PV_1(t), S_1(t+1): while warpgroup 1 runs its softmax the
+      // tensor core works for warpgroup 0 and vice versa.  S_g(t+1) overwrites the TMEM columns
+      // PV_g(t) reads; tcgen05.mma instructions issued by one thread execute in issue order, so the
+      // reads of PV_g(t) precede the writes of S_g(t+1) (FlashAttention-4's forward schedules the
+      // same pair the same way).  The commit of S_g(t+1) covers PV_g(t) as well, so a softmax
+      // warpgroup that sees S_g(t+1) complete may also rescale O_g.
+      bool ok = wait_bounded(bar(L::kBarQ), 0u, w, kStQFull);
+      if (ok) ok = issue_s(0, 0);
+      if (ok && n_t1 > 0) ok = issue_s(1, 0);
+      for (int t = 0; ok && t < n_t0; ++t) {
+        if (!(ok = issue_pv(0, t, t + 1 == n_t0))) break;
+        if (t + 1 < n_t0 && !(ok = issue_s(0, t + 1))) break;
+        if (t < n_t1) {
+          if (!(ok = issue_pv(1, t, t + 1 == n_t1))) break;
+          if (t + 1 < n_t1 && !(ok = issue_s(1, t + 1))) break;
+        }
       }
       // Exit path: all MMAs this thread issued must be complete before TMEM is freed.
       umma_commit(bar(L::kBarDrain));
       wait_drain(bar(L::kBarDrain), 0u, args.timeout_ns);
     }
     __syncwarp();
-  } else if (warp >= 4) {
-    // ------------------------------------------------------------------ softmax warpgroup
-    const int r = static_cast<int>(threadIdx.x) - kSoftmaxThread0;  // row within the tile
+  } else if (warp >= kSoftmaxWarp0) {
+    // ------------------------------------------------------------------ softmax warpgroups
+    const int g = (warp - kSoftmaxWarp0) >> 2;  // 0: even key tiles, 1: odd key tiles
+    const int n_t = g == 0 ? n_t0 : n_t1;
+    const int r = (warp & 3) * 32 + lane;  // row within the tile == TMEM lane
     const int row = q0 + r;
     const uint32_t tl = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    const uint32_t s_col = L::kColS + g * BN;
+    const uint32_t o_col = L::kColO + g * D;
     const float sl2 = args.scale_log2;
-    constexpr bool kRoundedNorm = std::is_same<T, __nv_bfloat16>::value;
     float m_ref = -INFINITY;  // max used in the exponents (raw score units)
-    float l_sum = 0.f;        // running sum of the fp32 weights (-> lse)
-    float lq_sum = 0.f;       // running sum of the rounded weights (bf16: -> 1/l of O)
+    float l_sum = 0.f;        // running sum of the fp32 weights
     bool ok = true;
-    for (int j = 0; j < n_tiles; ++j) {
-      ok = __all_sync(0xffffffffu, wait_bounded(bar(L::kBarSFull + (j & 1)),
-                                                static_cast<uint32_t>(j >> 1) & 1u, w, kStSFull));
+    for (int t = 0; t < n_t; ++t) {
+      const int j = 2 * t + g;
+      ok = __all_sync(0xffffffffu, wait_bounded(bar(L::kBarSFull + g),
+                                                static_cast<uint32_t>(t) & 1u, w, kStSFull));
       if (!ok) break;
       tc_fence_after();
       float s[BN];
-      const uint32_t scol = (j & 1) ? L::kColS1 : L::kColS0;
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t u[32];
-        tmem_ld32_wait(tl + scol + c * 32, u);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(u[i]);
-      }
+      load_s_row<BN>(tl + s_col, s);
       const int kv0 = j * BN;
       if ((CAUSAL && kv0 + BN - 1 > q0) || kv0 + BN > args.N) {
 #pragma unroll
@@ -365,91 +491,94 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (kv >= args.N || (CAUSAL && kv > row)) s[c] = -INFINITY;
         }
       }
-      float tmax = -INFINITY;
-#pragma unroll
-      for (int c = 0; c < BN; ++c) tmax = fmaxf(tmax, s[c]);
-      const float m_new = fmaxf(m_ref, tmax);
+      const float m_new = fmaxf(m_ref, row_max<BN>(s));
       const bool resc = (m_ref == -INFINITY) ? (m_new != -INFINITY)
                                              : ((m_new - m_ref) * sl2 > kRescaleThreshold);
       const float m_use = resc ? m_new : m_ref;
       const float alpha =
           resc ? ((m_ref == -INFINITY) ? 0.f : ex2_approx((m_ref - m_use) * sl2)) : 1.f;
       const float mc = (m_use == -INFINITY) ? 0.f : m_use * sl2;
-      float rs = 0.f;   // sum of the fp32 weights: the logsumexp uses this one
-      float rsq = 0.f;  // bf16 only: sum of the rounded weights, the normaliser of O
-      uint32_t pk[BN / 2];
-#pragma unroll
-      for (int c = 0; c < BN / 2; ++c) {
-        const float p0 = ex2_approx(fmaf(s[2 * c], sl2, -mc));
-        const float p1 = ex2_approx(fmaf(s[2 * c + 1], sl2, -mc));
-        pk[c] = pack2<T>(p0, p1);
-        rs += p0 + p1;
-        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-          // bf16 keeps 8 significant bits: O is normalised by the sum of the ROUNDED weights
-          // the tensor core multiplies, so o stays a convex combination of V rows and the
-          // common-mode part of the rounding error cancels (rows with few keys).
-          rsq += __uint_as_float(pk[c] << 16) + __uint_as_float(pk[c] & 0xFFFF0000u);
-        }
+      // P_g over the first half of S_g (all of S_g's row is in registers by now).
+      float rs;
+      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        rs = comp ? exp_pack_store<T, BN, true>(s, sl2, mc, tl + s_col)
+                  : exp_pack_store<T, BN, false>(s, sl2, mc, tl + s_col);
+      } else {
+        rs = exp_pack_store<T, BN, false>(s, sl2, mc, tl + s_col);
       }
-      const uint32_t pcol = (j & 1) ? L::kColP1 : L::kColP0;
-#pragma unroll
-      for (int c = 0; c < BN / 2; c += 16) tmem_st16(tl + pcol + c, &pk[c]);
       tmem_st_wait();
       l_sum = l_sum * alpha + rs;
-      if constexpr (kRoundedNorm) lq_sum = lq_sum * alpha + rsq;
       m_ref = m_use;
-      if (j > 0) {
-        // PV_{j-1} must be complete before O may be touched (and, for phase bookkeeping, it is
-        // waited for on every tile: it finished long ago in the common case).
-        ok = __all_sync(0xffffffffu, wait_bounded(bar(L::kBarODone),
-                                                  static_cast<uint32_t>(j - 1) & 1u, w, kStODone));
-        if (!ok) break;
-        if (__any_sync(0xffffffffu, resc)) {
-          tc_fence_after();
+      // O_g correction.  S_g(t) completing implies PV_g(t-1) completed (the commit of S_g(t)
+      // covers every MMA issued before it), and PV_g(t) waits for our arrival below.
+      if (t > 0 && __any_sync(0xffffffffu, resc)) {
 #pragma unroll
-          for (int c = 0; c < D; c += 32) {
-            uint32_t u[32];
-            tmem_ld32_wait(tl + L::kColO + c, u);
+        for (int c = 0; c < D; c += 32) {
+          uint32_t u[32];
+          tmem_ld32_wait(tl + o_col + c, u);
 #pragma unroll
-            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
-            tmem_st32(tl + L::kColO + c, u);
-          }
-          tmem_st_wait();
+          for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
+          tmem_st32(tl + o_col + c, u);
         }
+        tmem_st_wait();
       }
       tc_fence_before();
-      mbar_arrive(bar(L::kBarPFull + (j & 1)));
+      mbar_arrive(bar(L::kBarPFull + g));
     }
-    if (ok) {
-      ok = __all_sync(0xffffffffu, wait_bounded(bar(L::kBarODone),
-                                                static_cast<uint32_t>(n_tiles - 1) & 1u, w,
-                                                kStODone));
+    // ---- merge the two partials and write O / LSE ------------------------------------------
+    if (ok && n_t > 0) {  // committed once, after the warpgroup's last PV
+      ok = __all_sync(0xffffffffu, wait_bounded(bar(L::kBarPVDone + g), 0u, w, kStODone));
     }
-    if (ok) {
+    tc_fence_before();
+    // Barrier 1: both warpgroups' last PVs are complete, hence every MMA of the CTA is (the last
+    // one issued is one of the two), so the Q tile is free for the exchange.
+    named_barrier_sync(kMergeBarrier, 256);
+    float* xch = reinterpret_cast<float*>(smem + L::kQOff);
+    const bool live = (*abort_flag == 0);
+    if (live) {
+      xch[(g * 2 + 0) * kBlockM + r] = m_ref;
+      xch[(g * 2 + 1) * kBlockM + r] = l_sum;
+    }
+    named_barrier_sync(kMergeBarrier, 256);
+    if (live && *abort_flag == 0) {
       tc_fence_after();
-      const float l_norm = kRoundedNorm ? lq_sum : l_sum;
-      const float inv_l = (l_norm > 0.f) ? 1.f / l_norm : 0.f;
+      const float m0 = xch[0 * kBlockM + r], l0 = xch[1 * kBlockM + r];
+      const float m1 = xch[2 * kBlockM + r], l1 = xch[3 * kBlockM + r];
+      const float m = fmaxf(m0, m1);
+      const float a0 = (m0 == -INFINITY) ? 0.f : ex2_approx((m0 - m) * sl2);
+      const float a1 = (m1 == -INFINITY) ? 0.f : ex2_approx((m1 - m) * sl2);
+      const float l = l0 * a0 + l1 * a1;
+      const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
+      const float f0 = a0 * inv_l, f1 = a1 * inv_l;
       const bool in_range = row < args.N;
       T* orow = reinterpret_cast<T*>(args.o) +
                 (static_cast<size_t>(bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)) * D;
+      // Each warpgroup normalises and stores half of the head dimension.
 #pragma unroll
-      for (int c = 0; c < D; c += 32) {
-        uint32_t u[32];
-        tmem_ld32_wait(tl + L::kColO + c, u);
+      for (int c = g * (D / 2); c < (g + 1) * (D / 2); c += 32) {
+        uint32_t u0[32];
+        tmem_ld32_wait(tl + L::kColO + c, u0);
+        float o[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(u0[i]) * f0;
+        if (n_t1 > 0) {
+          uint32_t u1[32];
+          tmem_ld32_wait(tl + L::kColO + D + c, u1);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = fmaf(__uint_as_float(u1[i]), f1, o[i]);
+        }
         uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          pk[i] = pack2<T>(__uint_as_float(u[2 * i]) * inv_l, __uint_as_float(u[2 * i + 1]) * inv_l);
-        }
+        for (int i = 0; i < 16; ++i) pk[i] = pack2<T>(o[2 * i], o[2 * i + 1]);
         if (in_range) {
           uint4* dst = reinterpret_cast<uint4*>(orow + c);
 #pragma unroll
           for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
         }
       }
-      if (in_range) {
+      if (g == 0 && in_range) {
         args.lse[static_cast<size_t>(bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)] =
-            (l_sum > 0.f && m_ref != -INFINITY) ? fmaf(m_ref, args.scale, logf(l_sum)) : INFINITY;
+            (l > 0.f && m != -INFINITY) ? fmaf(m, args.scale, logf(l)) : INFINITY;
       }
     }
   }
@@ -556,7 +685,7 @@ cudaError_t launch_impl(const LaunchArgs& a, cudaStream_t stream) {
 template <typename T, int D>
 cudaError_t launch_d(const LaunchArgs& a, cudaStream_t s) {
   // STAGES per key-tile width: as deep as shared memory allows with one CTA per SM.
-  constexpr int kStages128 = (D == 128) ? 2 : 4;
+  constexpr int kStages128 = (D == 128) ? 3 : 4;
   switch (a.block_n) {
     case 128:
       return a.causal ? launch_impl<T, D, 128, kStages128, true>(a, s)
