@@ -9,14 +9,19 @@
 // Top-left causal: key tiles past the query tile's last row are never loaded
 // (stage5_tuned.cu:532-533); the diagonal tile is masked element-wise (:596-602).
 //
-// One CTA computes one 128-row query tile of one (batch, head).  Warp roles (384 threads):
-//   warp 0      TMA producer: Q once, then K_j / V_j through a STAGES-deep shared-memory ring
-//               (full/empty mbarrier pairs; K and V have separate slots so K_{j+STAGES} can land
-//               while V_j is still being read).
+// Persistent CTAs, one per SM (each needs all 512 TMEM columns and ~220 KB of shared memory), each
+// walking a fixed list of work items -- one 128-row query tile of one (batch, head) -- in a
+// balanced order (see decode_item).  Warp roles (384 threads):
+//   warp 0      TMA producer: each item's Q tile (after the previous item's S MMAs released the
+//               buffer) and the K tiles through a KST-deep ring (full/empty mbarrier pairs).
 //   warp 1      owns tensor memory (alloc/dealloc); lane 0 issues every tcgen05.mma.
-//   warps 2-3   idle (they only join the final barrier).
-//   warps 4-7   softmax warpgroup 0: key tiles j = 0, 2, 4, ...
-//   warps 8-11  softmax warpgroup 1: key tiles j = 1, 3, 5, ...
+//   warp 2      TMA producer of the V tiles through a VST-deep ring.
+//   warp 3      idle (it only joins the final barrier).
+//   warps 4-7   softmax warpgroup 0: key tiles j = 0, 2, 4, ... of each item
+//   warps 8-11  softmax warpgroup 1: key tiles j = 1, 3, 5, ... of each item
+// Barrier phases run on across items.  The next item's first S MMAs overlap the current item's
+// merge/store epilogue; its first PV (which overwrites O) waits for the o_free barrier that the
+// 256 softmax threads arrive on once they have read O_0 and O_1.
 // Each softmax warpgroup runs its own online softmax (own running max m_w and sums l_w) over its
 // half of the key tiles into its own accumulator O_w; one thread per query row (TMEM lane = row).
 // The two partial results are merged at the end exactly like two split-KV partials:
@@ -67,6 +72,23 @@ namespace fa_sm100 {
 __device__ unsigned int g_status;       // sticky cause bits of timed-out waits
 __device__ unsigned int g_abort_epoch;  // epoch of the last launch in which a wait ran out
 
+#ifdef FA_TRACE
+// Debug builds only: SM-clock timestamps of the first item of the first kTraceCtas CTAs, per
+// event kind e (0 S issued, 1 PV issued, 2 S seen by softmax, 3 P stored), group g, tile t.
+constexpr int kTraceCtas = 8, kTraceTiles = 64;
+__device__ long long g_trace[kTraceCtas][6][2][kTraceTiles];
+__device__ long long g_trace_t0[kTraceCtas];
+#define FA_TRACE_EV(first, e, g, t)                                                      \
+  do {                                                                                   \
+    if ((first) && blockIdx.x < kTraceCtas && (t) < kTraceTiles)                         \
+      g_trace[blockIdx.x][e][g][t] = clock64() - g_trace_t0[blockIdx.x];                 \
+  } while (0)
+#else
+#define FA_TRACE_EV(first, e, g, t) \
+  do {                              \
+  } while (0)
+#endif
+
 namespace {
 
 constexpr int kBlockM = 128;
@@ -75,7 +97,7 @@ constexpr int kSoftmaxWarp0 = 4;  // warps 4..11: two softmax warpgroups
 constexpr int kMergeBarrier = 1;  // named barrier id shared by the 256 softmax threads
 constexpr float kRescaleThreshold = 8.0f;
 
-template <int D, int BN, int STAGES>
+template <int D, int BN, int KST, int VST>
 struct Layout {
   static constexpr int kEB = 2;                  // bytes per element (fp16/bf16)
   static constexpr int kSwElems = 128 / kEB;     // elements per 128-byte swizzle row
@@ -86,16 +108,18 @@ struct Layout {
   static constexpr int kKVBytes = BN * D * kEB;
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kQBytes;
-  static constexpr int kVOff = kKOff + STAGES * kKVBytes;
-  static constexpr int kBarOff = kVOff + STAGES * kKVBytes;
-  static constexpr int kNumBars = 8 + 4 * STAGES;
+  static constexpr int kVOff = kKOff + KST * kKVBytes;
+  static constexpr int kXchOff = kVOff + VST * kKVBytes;  // merge exchange: m, l per row and group
+  static constexpr int kXchBytes = 2 * 2 * kBlockM * 4 + 16;
+  static constexpr int kBarOff = kXchOff + kXchBytes;
+  static constexpr int kNumBars = 10 + 2 * KST + 2 * VST;
   static constexpr int kMiscOff = kBarOff + 8 * kNumBars;
   static constexpr int kBytes = kMiscOff + 16;
   static constexpr int kSmemAlloc = kBytes + 1024;  // slack to align the base to 1024 bytes
 
   // Tensor memory columns.
-  static constexpr int kColS = 0;       // + w * BN
-  static constexpr int kColO = 2 * BN;  // + w * D
+  static constexpr int kColS = 0;       // + g * BN
+  static constexpr int kColO = 2 * BN;  // + g * D
   static constexpr int kColsUsed = 2 * BN + 2 * D;
   static constexpr int kTmemCols = kColsUsed <= 32    ? 32
                                    : kColsUsed <= 64  ? 64
@@ -104,19 +128,18 @@ struct Layout {
                                                       : 512;
 
   // Barrier indices.
-  static constexpr int kBarQ = 0;
-  static constexpr int kBarKFull = 1;                // + stage
-  static constexpr int kBarVFull = 1 + STAGES;       // + stage
-  static constexpr int kBarKEmpty = 1 + 2 * STAGES;  // + stage
-  static constexpr int kBarVEmpty = 1 + 3 * STAGES;  // + stage
-  static constexpr int kBarSFull = 1 + 4 * STAGES;   // + warpgroup
-  static constexpr int kBarPFull = 3 + 4 * STAGES;   // + warpgroup
-  static constexpr int kBarPVDone = 5 + 4 * STAGES;  // + warpgroup
-  static constexpr int kBarDrain = 7 + 4 * STAGES;
+  static constexpr int kBarQFull = 0;
+  static constexpr int kBarQEmpty = 1;
+  static constexpr int kBarSFull = 2;   // + group
+  static constexpr int kBarPFull = 4;   // + group
+  static constexpr int kBarPVDone = 6;  // + group
+  static constexpr int kBarOFree = 8;
+  static constexpr int kBarDrain = 9;
+  static constexpr int kBarKFull = 10;                   // + stage
+  static constexpr int kBarKEmpty = 10 + KST;            // + stage
+  static constexpr int kBarVFull = 10 + 2 * KST;         // + stage
+  static constexpr int kBarVEmpty = 10 + 2 * KST + VST;  // + stage
 
-  // The merge exchange (m, l per row and warpgroup) reuses the Q tile once every MMA is done.
-  static constexpr int kMergeFloats = 2 * 2 * kBlockM;
-  static_assert(kMergeFloats * 4 <= kQBytes, "merge exchange must fit in the Q tile");
   static_assert(D % kSwElems == 0, "D must be a multiple of the swizzle width");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 128, "BN must be 32, 64 or 128");
   static_assert(kColsUsed <= 512, "tensor memory overflow");
@@ -128,13 +151,41 @@ struct KArgs {
   float* lse;
   int H, Hkv, N;
   int n_q_tiles;
-  int head_major;  // 1: consecutive CTAs walk the query tiles of one head (L2 reuse of K/V)
+  int n_bh;        // B * H
+  int n_items;     // n_bh * n_q_tiles work items (one 128-row query tile of one head each)
+  int head_major;  // 1: the item order walks the query tiles of one head (L2 reuse of K/V)
   float scale;
   float scale_log2;
   unsigned long long timeout_ns;
   unsigned int epoch;
   int skip_kv_tile;
 };
+
+// Work items are visited in a fixed order -- heaviest causal query tiles first (longest
+// processing time first), all heads interleaved, or head by head when K/V of all heads would
+// not stay in L2 -- and dealt to the persistent CTAs boustrophedon-wise: round r gives item
+// r*G + c to CTA c on even rounds and r*G + (G-1-c) on odd ones, which pairs heavy with light
+// items across rounds.
+struct Item {
+  int bh, q_tile;
+};
+
+__device__ __forceinline__ int item_index(int round, int G, int c) {
+  return round * G + ((round & 1) ? (G - 1 - c) : c);
+}
+
+template <bool CAUSAL>
+__device__ __forceinline__ Item decode_item(int i, const KArgs& a) {
+  int bh, qr;
+  if (a.head_major) {
+    bh = i / a.n_q_tiles;
+    qr = i - bh * a.n_q_tiles;
+  } else {
+    qr = i / a.n_bh;
+    bh = i - qr * a.n_bh;
+  }
+  return Item{bh, CAUSAL ? a.n_q_tiles - 1 - qr : qr};
+}
 
 struct WaitCtx {
   volatile int* abort_flag;
@@ -202,39 +253,41 @@ __device__ __forceinline__ void load_s_row(uint32_t taddr, float (&s)[BN]) {
   for (int i = 0; i < BN; ++i) s[i] = __uint_as_float(u[i]);
 }
 
-// Row maximum with four independent three-input max chains (BN/8 deep instead of BN).
+// Row maximum with eight independent three-input max chains (BN/16 deep instead of BN).
 template <int BN>
 __device__ __forceinline__ float row_max(const float (&s)[BN]) {
-  float a0 = fmaxf(s[0], s[1]), a1 = fmaxf(s[2], s[3]);
-  float a2 = fmaxf(s[4], s[5]), a3 = fmaxf(s[6], s[7]);
+  float a[8];
 #pragma unroll
-  for (int i = 8; i < BN; i += 8) {
-    a0 = fmax3(a0, s[i + 0], s[i + 1]);
-    a1 = fmax3(a1, s[i + 2], s[i + 3]);
-    a2 = fmax3(a2, s[i + 4], s[i + 5]);
-    a3 = fmax3(a3, s[i + 6], s[i + 7]);
+  for (int k = 0; k < 8; ++k) a[k] = fmaxf(s[2 * k], s[2 * k + 1]);
+#pragma unroll
+  for (int i = 16; i < BN; i += 16) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k) a[k] = fmax3(a[k], s[i + 2 * k], s[i + 2 * k + 1]);
   }
-  return fmax3(fmaxf(a0, a1), a2, a3);
+  return fmax3(fmax3(a[0], a[1], a[2]), fmax3(a[3], a[4], a[5]), fmaxf(a[6], a[7]));
 }
 
-// p = 2^(s*c - m*c) for one S row: the exponent argument in packed fp32 pairs, the exponential
-// on MUFU (and every kEmuEvery-th pair on the FMA pipes), P packed two per 32-bit word and stored
-// to TMEM at `taddr` (BN/2 columns).  Returns the row sum of the fp32 weights, accumulated in
-// four packed partial sums.  kLo (bf16 only) also stores P_lo = p - bf16(p) in the next BN/2
-// columns.
-template <typename T, int BN, bool kLo>
+// p = 2^(s*c - m*c) for columns [2*C0, 2*C1) of one S row: the exponent argument in packed fp32
+// pairs, the exponential on MUFU (every kEmuEvery-th pair on the FMA pipes), P packed two per
+// 32-bit word and stored to TMEM at `taddr` + C0 (one column per pair).  Returns the sum of the
+// fp32 weights, accumulated in four packed partial sums.  kLo (bf16 only) also stores
+// P_lo = p - bf16(p) at `taddr` + BN/2 + C0.
+template <typename T, int BN, int C0, int C1, bool kLo>
 __device__ __forceinline__ float exp_pack_store(const float (&s)[BN], float sl2, float mc,
                                                 uint32_t taddr) {
+  static_assert((C1 - C0) % 16 == 0, "column range must be a multiple of 16 pairs");
+  constexpr int kN = C1 - C0;
   const uint64_t c2 = f2_pack(sl2, sl2);
   const uint64_t nb2 = f2_pack(-mc, -mc);
   uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-  uint32_t pk[BN / 2];
-  uint32_t lo[kLo ? BN / 2 : 1];
+  uint32_t pk[kN];
+  uint32_t lo[kLo ? kN : 1];
 #pragma unroll
-  for (int c = 0; c < BN / 2; ++c) {
-    const uint64_t x = f2_fma(f2_pack(s[2 * c], s[2 * c + 1]), c2, nb2);
+  for (int c = 0; c < kN; ++c) {
+    const int cc = C0 + c;
+    const uint64_t x = f2_fma(f2_pack(s[2 * cc], s[2 * cc + 1]), c2, nb2);
     float p0, p1;
-    if (kEmuEvery > 0 && (c % (kEmuEvery > 0 ? kEmuEvery : 1)) == (kEmuEvery > 0 ? kEmuEvery : 1) - 1) {
+    if (kEmuEvery > 0 && (cc % (kEmuEvery > 0 ? kEmuEvery : 1)) == (kEmuEvery > 0 ? kEmuEvery : 1) - 1) {
       p0 = ex2_poly3(f2_lo(x));
       p1 = ex2_poly3(f2_hi(x));
     } else {
@@ -248,10 +301,10 @@ __device__ __forceinline__ float exp_pack_store(const float (&s)[BN], float sl2,
     }
   }
 #pragma unroll
-  for (int c = 0; c < BN / 2; c += 16) tmem_st16(taddr + c, &pk[c]);
+  for (int c = 0; c < kN; c += 16) tmem_st16(taddr + C0 + c, &pk[c]);
   if constexpr (kLo) {
 #pragma unroll
-    for (int c = 0; c < BN / 2; c += 16) tmem_st16(taddr + BN / 2 + c, &lo[c]);
+    for (int c = 0; c < kN; c += 16) tmem_st16(taddr + BN / 2 + C0 + c, &lo[c]);
   }
   const uint64_t t = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
   return f2_lo(t) + f2_hi(t);
@@ -261,12 +314,12 @@ __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
 
-template <typename T, int D, int BN, int STAGES, bool CAUSAL>
+template <typename T, int D, int BN, int KST, int VST, bool CAUSAL>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const KArgs args) {
-  using L = Layout<D, BN, STAGES>;
+  using L = Layout<D, BN, KST, VST>;
   constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
 
   extern __shared__ uint8_t smem_raw[];
@@ -279,47 +332,31 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-
-  // Work item: (batch*head, query tile).  Heaviest causal tiles first (longest processing time
-  // first keeps the tail short); head-major order when K/V of all heads would not stay in L2.
-  int bh, q_tile_rev;
-  if (args.head_major) {
-    bh = static_cast<int>(blockIdx.x) / args.n_q_tiles;
-    q_tile_rev = static_cast<int>(blockIdx.x) % args.n_q_tiles;
-  } else {
-    const int n_bh = static_cast<int>(gridDim.x) / args.n_q_tiles;
-    bh = static_cast<int>(blockIdx.x) % n_bh;
-    q_tile_rev = static_cast<int>(blockIdx.x) / n_bh;
-  }
-  const int q_tile = CAUSAL ? (args.n_q_tiles - 1 - q_tile_rev) : q_tile_rev;
-  const int q0 = q_tile * kBlockM;
-  const int b_idx = bh / args.H;
-  const int h_idx = bh - b_idx * args.H;
-  const int bh_kv = b_idx * args.Hkv + h_idx / (args.H / args.Hkv);
-  const int kv_end = CAUSAL ? min(args.N, q0 + kBlockM) : args.N;
-  const int n_tiles = (kv_end + BN - 1) / BN;  // >= 1
-  const int n_t0 = (n_tiles + 1) / 2;          // tiles of warpgroup 0 (even j)
-  const int n_t1 = n_tiles / 2;                // tiles of warpgroup 1 (odd j)
-  // bf16 keeps 8 significant bits.  In the first causal query tile the rows average only a
-  // handful of keys, so rounding P to bf16 would add up to ~2^-9 |v| on top of the output
-  // rounding; there P is carried as P_hi + P_lo (two bf16 MMAs).  Everywhere else a row averages
-  // >= 128 keys and the rounding errors average out.
-  const bool comp = std::is_same<T, __nv_bfloat16>::value && CAUSAL && q_tile == 0;
+  const int G = static_cast<int>(gridDim.x);
+  const int cta = static_cast<int>(blockIdx.x);
 
   if (threadIdx.x == 0) {
-    mbar_init(bar(L::kBarQ), 1);
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(bar(L::kBarKFull + s), 1);
-      mbar_init(bar(L::kBarVFull + s), 1);
-      mbar_init(bar(L::kBarKEmpty + s), 1);
-      mbar_init(bar(L::kBarVEmpty + s), 1);
-    }
+#ifdef FA_TRACE
+    if (blockIdx.x < kTraceCtas) g_trace_t0[blockIdx.x] = clock64();
+#endif
+    mbar_init(bar(L::kBarQFull), 1);
+    mbar_init(bar(L::kBarQEmpty), 1);
     for (int g = 0; g < 2; ++g) {
       mbar_init(bar(L::kBarSFull + g), 1);
       mbar_init(bar(L::kBarPFull + g), kBlockM);
+
       mbar_init(bar(L::kBarPVDone + g), 1);
     }
+    mbar_init(bar(L::kBarOFree), 2 * kBlockM);
     mbar_init(bar(L::kBarDrain), 1);
+    for (int s = 0; s < KST; ++s) {
+      mbar_init(bar(L::kBarKFull + s), 1);
+      mbar_init(bar(L::kBarKEmpty + s), 1);
+    }
+    for (int s = 0; s < VST; ++s) {
+      mbar_init(bar(L::kBarVFull + s), 1);
+      mbar_init(bar(L::kBarVEmpty + s), 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -333,52 +370,75 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   const WaitCtx w{abort_flag, args.timeout_ns, args.epoch};
 
-  if (warp == 0) {
-    // ------------------------------------------------------------------ TMA producer
+  if (warp == 0 || warp == 2) {
+    // ------------------------------------------------------------------ TMA producers
+    // warp 0: Q of every item and the K ring; warp 2: the V ring.  Each walks the CTA's items.
     if (lane == 0) {
-      tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(&tm_k);
-      tma_prefetch_desc(&tm_v);
-      mbar_arrive_expect_tx(bar(L::kBarQ), L::kQBytes);
-#pragma unroll
-      for (int c = 0; c < L::kDChunks; ++c) {
-        tma_load_3d(sbase + L::kQOff + c * L::kQChunkBytes, &tm_q, c * L::kSwElems, q0, bh,
-                    bar(L::kBarQ));
-      }
-      int k_issued = 0, v_issued = 0;
-      for (int j = 0; j < n_tiles; ++j) {
-        const int s = j % STAGES;
-        const uint32_t ph = static_cast<uint32_t>(j / STAGES) & 1u;
-        if (j >= STAGES && !wait_bounded(bar(L::kBarKEmpty + s), ph ^ 1u, w, kStKVEmpty)) break;
-        if (j != args.skip_kv_tile) {
-          mbar_arrive_expect_tx(bar(L::kBarKFull + s), L::kKVBytes);
+      const bool is_k = (warp == 0);
+      constexpr int kStMax = KST > VST ? KST : VST;
+      const int nst = is_k ? KST : VST;
+      const int bar_full = is_k ? L::kBarKFull : L::kBarVFull;
+      const int bar_empty = is_k ? L::kBarKEmpty : L::kBarVEmpty;
+      const uint32_t ring = sbase + (is_k ? L::kKOff : L::kVOff);
+      const CUtensorMap* tm = is_k ? &tm_k : &tm_v;
+      if (is_k) tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(tm);
+      int count = 0;        // tiles this producer has issued, over all items
+      int items_done = 0;   // items whose Q this producer loaded (warp 0)
+      unsigned skipped = 0;  // bit (count % 32): that tile's copy was skipped (fault injection)
+      bool ok = true;
+      for (int r = 0; ok; ++r) {
+        const int i = item_index(r, G, cta);
+        if (i >= args.n_items) break;
+        const Item item = decode_item<CAUSAL>(i, args);
+        const int q0 = item.q_tile * kBlockM;
+        const int b_idx = item.bh / args.H;
+        const int bh_kv = b_idx * args.Hkv + (item.bh - b_idx * args.H) / (args.H / args.Hkv);
+        const int kv_end = CAUSAL ? min(args.N, q0 + kBlockM) : args.N;
+        const int n_tiles = (kv_end + BN - 1) / BN;
+        if (is_k) {
+          // The previous item's S MMAs must be done with the Q buffer.
+          if (items_done > 0 &&
+              !(ok = wait_bounded(bar(L::kBarQEmpty), static_cast<uint32_t>(items_done - 1) & 1u,
+                                  w, kStKVEmpty))) {
+            break;
+          }
+          mbar_arrive_expect_tx(bar(L::kBarQFull), L::kQBytes);
 #pragma unroll
           for (int c = 0; c < L::kDChunks; ++c) {
-            tma_load_3d(sbase + L::kKOff + s * L::kKVBytes + c * L::kKVChunkBytes, &tm_k,
-                        c * L::kSwElems, j * BN, bh_kv, bar(L::kBarKFull + s));
+            tma_load_3d(sbase + L::kQOff + c * L::kQChunkBytes, &tm_q, c * L::kSwElems, q0,
+                        item.bh, bar(L::kBarQFull));
+          }
+          ++items_done;
+        }
+        for (int j = 0; j < n_tiles; ++j, ++count) {
+          const int s = count % nst;
+          const uint32_t ph = static_cast<uint32_t>(count / nst) & 1u;
+          if (count >= nst && !(ok = wait_bounded(bar(bar_empty + s), ph ^ 1u, w, kStKVEmpty))) {
+            break;
+          }
+          if (is_k && j == args.skip_kv_tile) {
+            skipped |= 1u << (count & 31);
+            continue;
+          }
+          skipped &= ~(1u << (count & 31));
+          mbar_arrive_expect_tx(bar(bar_full + s), L::kKVBytes);
+#pragma unroll
+          for (int c = 0; c < L::kDChunks; ++c) {
+            tma_load_3d(ring + s * L::kKVBytes + c * L::kKVChunkBytes, tm, c * L::kSwElems,
+                        j * BN, bh_kv, bar(bar_full + s));
           }
         }
-        k_issued = j + 1;
-        if (j >= STAGES && !wait_bounded(bar(L::kBarVEmpty + s), ph ^ 1u, w, kStKVEmpty)) break;
-        mbar_arrive_expect_tx(bar(L::kBarVFull + s), L::kKVBytes);
-#pragma unroll
-        for (int c = 0; c < L::kDChunks; ++c) {
-          tma_load_3d(sbase + L::kVOff + s * L::kKVBytes + c * L::kKVChunkBytes, &tm_v,
-                      c * L::kSwElems, j * BN, bh_kv, bar(L::kBarVFull + s));
-        }
-        v_issued = j + 1;
       }
+      (void)kStMax;
       // Exit path: every copy this thread started must have landed before the CTA may exit.
-      wait_drain(bar(L::kBarQ), 0u, args.timeout_ns);
-      for (int j = (k_issued > STAGES ? k_issued - STAGES : 0); j < k_issued; ++j) {
-        if (j != args.skip_kv_tile) {
-          wait_drain(bar(L::kBarKFull + j % STAGES), static_cast<uint32_t>(j / STAGES) & 1u,
-                     args.timeout_ns);
-        }
+      if (is_k && items_done > 0) {
+        wait_drain(bar(L::kBarQFull), static_cast<uint32_t>(items_done - 1) & 1u, args.timeout_ns);
       }
-      for (int j = (v_issued > STAGES ? v_issued - STAGES : 0); j < v_issued; ++j) {
-        wait_drain(bar(L::kBarVFull + j % STAGES), static_cast<uint32_t>(j / STAGES) & 1u,
-                   args.timeout_ns);
+      for (int c = (count > nst ? count - nst : 0); c < count; ++c) {
+        if (!((skipped >> (c & 31)) & 1u)) {
+          wait_drain(bar(bar_full + c % nst), static_cast<uint32_t>(c / nst) & 1u, args.timeout_ns);
+        }
       }
     }
   } else if (warp == 1) {
@@ -386,76 +446,107 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       constexpr uint32_t kIdescS = idesc_mma(kFmt, kBlockM, BN, false);
       constexpr uint32_t kIdescPV = idesc_mma(kFmt, kBlockM, D, true);
-      // S_g(t) = Q K_j^T, j = 2t + g, into S_g.
-      auto issue_s = [&](int g, int t) -> bool {
-        const int j = 2 * t + g;
-        const int s = j % STAGES;
-        if (!wait_bounded(bar(L::kBarKFull + s), static_cast<uint32_t>(j / STAGES) & 1u, w,
-                          kStKFull)) {
-          return false;
-        }
-        tc_fence_after();
-        const uint32_t d_tmem = tmem + L::kColS + g * BN;
-        const uint32_t kb = sbase + L::kKOff + s * L::kKVBytes;
+      // Descriptor bases; an offset inside a tile is added to the start-address field (the sum
+      // stays below 2^14 in 16-byte units for any shared-memory address, so it cannot carry).
+      const uint64_t q_desc0 = sdesc_sw128(sbase + L::kQOff, 16, 1024);
+      const uint64_t k_desc0 = sdesc_sw128(sbase + L::kKOff, 16, 1024);
+      const uint64_t v_desc0 = sdesc_sw128(sbase + L::kVOff, L::kKVChunkBytes, 1024);
+      int kc = 0, vc = 0;   // K / V tiles consumed, over all items
+      int pc[2] = {0, 0};   // P tiles consumed per group, over all items
+      int it = 0;           // items processed
+      bool ok = true;
+      for (int r = 0; ok; ++r) {
+        const int i = item_index(r, G, cta);
+        if (i >= args.n_items) break;
+        const Item item = decode_item<CAUSAL>(i, args);
+        const int q0 = item.q_tile * kBlockM;
+        const int kv_end = CAUSAL ? min(args.N, q0 + kBlockM) : args.N;
+        const int n_tiles = (kv_end + BN - 1) / BN;
+        const int n_t0 = (n_tiles + 1) / 2, n_t1 = n_tiles / 2;
+        const bool comp = std::is_same<T, __nv_bfloat16>::value && CAUSAL && item.q_tile == 0;
+        int s_issued = 0;  // S MMAs of this item
+        // S_g = Q K_j^T into S_g; the commit after the item's last S releases the Q buffer.
+        auto issue_s = [&](int g, int t) -> bool {
+          const int s = kc % KST;
+          if (!wait_bounded(bar(L::kBarKFull + s), static_cast<uint32_t>(kc / KST) & 1u, w,
+                            kStKFull)) {
+            return false;
+          }
+          tc_fence_after();
+          FA_TRACE_EV(it == 0, 0, g, t);
+          const uint32_t d_tmem = tmem + L::kColS + g * BN;
+          const uint64_t k_desc = k_desc0 + static_cast<uint64_t>((s * L::kKVBytes) >> 4);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const uint32_t q_off = (kk / 4) * L::kQChunkBytes + (kk % 4) * 32;
-          const uint32_t k_off = (kk / 4) * L::kKVChunkBytes + (kk % 4) * 32;
-          umma_ss(d_tmem, sdesc_sw128(sbase + L::kQOff + q_off, 16, 1024),
-                  sdesc_sw128(kb + k_off, 16, 1024), kIdescS, kk > 0 ? 1u : 0u);
-        }
-        umma_commit(bar(L::kBarSFull + g));
-        umma_commit(bar(L::kBarKEmpty + s));
-        return true;
-      };
-      // O_g += P_g V_j, j = 2t + g.  With `comp` (bf16 causal query tile 0) P_g is two bf16
-      // halves P_hi + P_lo in the two halves of S_g, and both are multiplied.
-      auto issue_pv = [&](int g, int t, bool last) -> bool {
-        const int j = 2 * t + g;
-        const int s = j % STAGES;
-        if (!wait_bounded(bar(L::kBarPFull + g), static_cast<uint32_t>(t) & 1u, w, kStPFull)) {
-          return false;
-        }
-        if (!wait_bounded(bar(L::kBarVFull + s), static_cast<uint32_t>(j / STAGES) & 1u, w,
-                          kStVFull)) {
-          return false;
-        }
-        tc_fence_after();
-        const uint32_t vb = sbase + L::kVOff + s * L::kKVBytes;
-        const uint32_t pa = tmem + L::kColS + g * BN;
-        const uint32_t o_tmem = tmem + L::kColO + g * D;
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          umma_ts(o_tmem, pa + kk * 8, sdesc_sw128(vb + kk * 16 * 128, L::kKVChunkBytes, 1024),
-                  kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
-        }
-        if (comp) {
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t q_off = (kk / 4) * L::kQChunkBytes + (kk % 4) * 32;
+            const uint32_t k_off = (kk / 4) * L::kKVChunkBytes + (kk % 4) * 32;
+            umma_ss(d_tmem, q_desc0 + (q_off >> 4), k_desc + (k_off >> 4), kIdescS,
+                    kk > 0 ? 1u : 0u);
+          }
+          umma_commit(bar(L::kBarSFull + g));
+          umma_commit(bar(L::kBarKEmpty + s));
+          ++kc;
+          if (++s_issued == n_tiles) umma_commit(bar(L::kBarQEmpty));
+          return true;
+        };
+        // O_g += P_g V_j (twice with `comp`: P_hi then P_lo from the second half of S_g).
+        auto issue_pv = [&](int g, int t, bool last) -> bool {
+          const int s = vc % VST;
+          if (!wait_bounded(bar(L::kBarPFull + g), static_cast<uint32_t>(pc[g]) & 1u, w,
+                            kStPFull)) {
+            return false;
+          }
+          ++pc[g];
+          if (!wait_bounded(bar(L::kBarVFull + s), static_cast<uint32_t>(vc / VST) & 1u, w,
+                            kStVFull)) {
+            return false;
+          }
+          tc_fence_after();
+          FA_TRACE_EV(it == 0, 1, g, t);
+          const uint64_t v_desc = v_desc0 + static_cast<uint64_t>((s * L::kKVBytes) >> 4);
+          const uint32_t pa = tmem + L::kColS + g * BN;
+          const uint32_t o_tmem = tmem + L::kColO + g * D;
 #pragma unroll
           for (int kk = 0; kk < BN / 16; ++kk) {
-            umma_ts(o_tmem, pa + BN / 2 + kk * 8,
-                    sdesc_sw128(vb + kk * 16 * 128, L::kKVChunkBytes, 1024), kIdescPV, 1u);
+            umma_ts(o_tmem, pa + kk * 8, v_desc + ((kk * 16 * 128) >> 4), kIdescPV,
+                    (t > 0 || kk > 0) ? 1u : 0u);
+          }
+          if (comp) {
+#pragma unroll
+            for (int kk = 0; kk < BN / 16; ++kk) {
+              umma_ts(o_tmem, pa + BN / 2 + kk * 8, v_desc + ((kk * 16 * 128) >> 4), kIdescPV, 1u);
+            }
+          }
+          if (last) umma_commit(bar(L::kBarPVDone + g));
+          umma_commit(bar(L::kBarVEmpty + s));
+          ++vc;
+          return true;
+        };
+        // Order: S_0(0), S_1(0), then per round PV_0(t), S_0(t+1), PV_1(t), S_1(t+1): the tensor
+        // core works for one group while the other runs its softmax.  S_g(t+1) overwrites the
+        // TMEM columns PV_g(t) reads right after it; tcgen05.mma instructions issued by one
+        // thread execute in issue order, so the reads come first (FlashAttention-4's forward
+        // schedules the same pair the same way).  The first S of an item may overlap the
+        // previous item's epilogue (S and O are distinct columns); its first PV (which
+        // overwrites O_g) waits until that epilogue has read both O_g.
+        if (!(ok = wait_bounded(bar(L::kBarQFull), static_cast<uint32_t>(it) & 1u, w, kStQFull))) {
+          break;
+        }
+        if (!(ok = issue_s(0, 0))) break;
+        if (n_t1 > 0 && !(ok = issue_s(1, 0))) break;
+        if (it > 0 && !(ok = wait_bounded(bar(L::kBarOFree), static_cast<uint32_t>(it - 1) & 1u,
+                                          w, kStODone))) {
+          break;
+        }
+        for (int t = 0; ok && t < n_t0; ++t) {
+          if (!(ok = issue_pv(0, t, t + 1 == n_t0))) break;
+          if (t + 1 < n_t0 && !(ok = issue_s(0, t + 1))) break;
+          if (t < n_t1) {
+            if (!(ok = issue_pv(1, t, t + 1 == n_t1))) break;
+            if (t + 1 < n_t1 && !(ok = issue_s(1, t + 1))) break;
           }
         }
-        if (last) umma_commit(bar(L::kBarPVDone + g));
-        umma_commit(bar(L::kBarVEmpty + s));
-        return true;
-      };
-      // Issue order PV_0(t), S_0(t+1), PV_1(t), S_1(t+1): while warpgroup 1 runs its softmax the
-      // tensor core works for warpgroup 0 and vice versa.  S_g(t+1) overwrites the TMEM columns
-      // PV_g(t) reads; tcgen05.mma instructions issued by one thread execute in issue order, so the
-      // reads of PV_g(t) precede the writes of S_g(t+1) (FlashAttention-4's forward schedules the
-      // same pair the same way).  The commit of S_g(t+1) covers PV_g(t) as well, so a softmax
-      // warpgroup that sees S_g(t+1) complete may also rescale O_g.
-      bool ok = wait_bounded(bar(L::kBarQ), 0u, w, kStQFull);
-      if (ok) ok = issue_s(0, 0);
-      if (ok && n_t1 > 0) ok = issue_s(1, 0);
-      for (int t = 0; ok && t < n_t0; ++t) {
-        if (!(ok = issue_pv(0, t, t + 1 == n_t0))) break;
-        if (t + 1 < n_t0 && !(ok = issue_s(0, t + 1))) break;
-        if (t < n_t1) {
-          if (!(ok = issue_pv(1, t, t + 1 == n_t1))) break;
-          if (t + 1 < n_t1 && !(ok = issue_s(1, t + 1))) break;
-        }
+        ++it;
       }
       // Exit path: all MMAs this thread issued must be complete before TMEM is freed.
       umma_commit(bar(L::kBarDrain));
@@ -465,82 +556,99 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp >= kSoftmaxWarp0) {
     // ------------------------------------------------------------------ softmax warpgroups
     const int g = (warp - kSoftmaxWarp0) >> 2;  // 0: even key tiles, 1: odd key tiles
-    const int n_t = g == 0 ? n_t0 : n_t1;
-    const int r = (warp & 3) * 32 + lane;  // row within the tile == TMEM lane
-    const int row = q0 + r;
+    const int r = (warp & 3) * 32 + lane;       // row within the tile == TMEM lane
     const uint32_t tl = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     const uint32_t s_col = L::kColS + g * BN;
     const uint32_t o_col = L::kColO + g * D;
     const float sl2 = args.scale_log2;
-    float m_ref = -INFINITY;  // max used in the exponents (raw score units)
-    float l_sum = 0.f;        // running sum of the fp32 weights
-    bool ok = true;
-    for (int t = 0; t < n_t; ++t) {
-      const int j = 2 * t + g;
-      ok = __all_sync(0xffffffffu, wait_bounded(bar(L::kBarSFull + g),
-                                                static_cast<uint32_t>(t) & 1u, w, kStSFull));
-      if (!ok) break;
-      tc_fence_after();
-      float s[BN];
-      load_s_row<BN>(tl + s_col, s);
-      const int kv0 = j * BN;
-      if ((CAUSAL && kv0 + BN - 1 > q0) || kv0 + BN > args.N) {
+    float* xch = reinterpret_cast<float*>(smem + L::kXchOff);
+    volatile int* xch_ctl = reinterpret_cast<volatile int*>(smem + L::kXchOff + 2 * 2 * kBlockM * 4);
+    int sc = 0;   // S tiles consumed by this group, over all items
+    int pvc = 0;  // item-final PV completions consumed by this group
+    for (int rnd = 0;; ++rnd) {
+      const int i = item_index(rnd, G, cta);
+      if (i >= args.n_items) break;
+      const Item item = decode_item<CAUSAL>(i, args);
+      const int q0 = item.q_tile * kBlockM;
+      const int row = q0 + r;
+      const int kv_end = CAUSAL ? min(args.N, q0 + kBlockM) : args.N;
+      const int n_tiles = (kv_end + BN - 1) / BN;
+      const int n_t1 = n_tiles / 2;
+      const int n_t = (g == 0) ? (n_tiles + 1) / 2 : n_t1;
+      const bool comp = std::is_same<T, __nv_bfloat16>::value && CAUSAL && item.q_tile == 0;
+      float m_ref = -INFINITY;  // max used in the exponents (raw score units)
+      float l_sum = 0.f;        // running sum of the fp32 weights
+      bool ok = true;
+      for (int t = 0; t < n_t; ++t) {
+        const int j = 2 * t + g;
+        ok = __all_sync(0xffffffffu, wait_bounded(bar(L::kBarSFull + g),
+                                                  static_cast<uint32_t>(sc) & 1u, w, kStSFull));
+        if (!ok) break;
+        ++sc;
+        tc_fence_after();
+        FA_TRACE_EV(rnd == 0 && r == 0, 2, g, t);
+        float s[BN];
+        load_s_row<BN>(tl + s_col, s);
+        FA_TRACE_EV(rnd == 0 && r == 0, 4, g, t);
+        const int kv0 = j * BN;
+        if ((CAUSAL && kv0 + BN - 1 > q0) || kv0 + BN > args.N) {
 #pragma unroll
-        for (int c = 0; c < BN; ++c) {
-          const int kv = kv0 + c;
-          if (kv >= args.N || (CAUSAL && kv > row)) s[c] = -INFINITY;
+          for (int c = 0; c < BN; ++c) {
+            const int kv = kv0 + c;
+            if (kv >= args.N || (CAUSAL && kv > row)) s[c] = -INFINITY;
+          }
         }
-      }
-      const float m_new = fmaxf(m_ref, row_max<BN>(s));
-      const bool resc = (m_ref == -INFINITY) ? (m_new != -INFINITY)
-                                             : ((m_new - m_ref) * sl2 > kRescaleThreshold);
-      const float m_use = resc ? m_new : m_ref;
-      const float alpha =
-          resc ? ((m_ref == -INFINITY) ? 0.f : ex2_approx((m_ref - m_use) * sl2)) : 1.f;
-      const float mc = (m_use == -INFINITY) ? 0.f : m_use * sl2;
-      // P_g over the first half of S_g (all of S_g's row is in registers by now).
-      float rs;
-      if constexpr (std::is_same<T, __nv_bfloat16>::value) {
-        rs = comp ? exp_pack_store<T, BN, true>(s, sl2, mc, tl + s_col)
-                  : exp_pack_store<T, BN, false>(s, sl2, mc, tl + s_col);
-      } else {
-        rs = exp_pack_store<T, BN, false>(s, sl2, mc, tl + s_col);
-      }
-      tmem_st_wait();
-      l_sum = l_sum * alpha + rs;
-      m_ref = m_use;
-      // O_g correction.  S_g(t) completing implies PV_g(t-1) completed (the commit of S_g(t)
-      // covers every MMA issued before it), and PV_g(t) waits for our arrival below.
-      if (t > 0 && __any_sync(0xffffffffu, resc)) {
-#pragma unroll
-        for (int c = 0; c < D; c += 32) {
-          uint32_t u[32];
-          tmem_ld32_wait(tl + o_col + c, u);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
-          tmem_st32(tl + o_col + c, u);
+        const float m_new = fmaxf(m_ref, row_max<BN>(s));
+        const bool resc = (m_ref == -INFINITY) ? (m_new != -INFINITY)
+                                               : ((m_new - m_ref) * sl2 > kRescaleThreshold);
+        const float m_use = resc ? m_new : m_ref;
+        const float alpha =
+            resc ? ((m_ref == -INFINITY) ? 0.f : ex2_approx((m_ref - m_use) * sl2)) : 1.f;
+        const float mc = (m_use == -INFINITY) ? 0.f : m_use * sl2;
+        FA_TRACE_EV(rnd == 0 && r == 0, 5, g, t);
+        // P_g over the first half of S_g (all of S_g's row is in registers by now).
+        float rs;
+        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+          rs = comp ? exp_pack_store<T, BN, 0, BN / 2, true>(s, sl2, mc, tl + s_col)
+                    : exp_pack_store<T, BN, 0, BN / 2, false>(s, sl2, mc, tl + s_col);
+        } else {
+          rs = exp_pack_store<T, BN, 0, BN / 2, false>(s, sl2, mc, tl + s_col);
         }
         tmem_st_wait();
+        l_sum = l_sum * alpha + rs;
+        m_ref = m_use;
+        // O_g correction.  S_g(t) completing implies PV_g(t-1) completed (the commit of S_g(t)
+        // covers every MMA issued before it), and PV_g(t) waits for our arrival below.
+        if (t > 0 && __any_sync(0xffffffffu, resc)) {
+#pragma unroll
+          for (int c = 0; c < D; c += 32) {
+            uint32_t u[32];
+            tmem_ld32_wait(tl + o_col + c, u);
+#pragma unroll
+            for (int k2 = 0; k2 < 32; ++k2) u[k2] = __float_as_uint(__uint_as_float(u[k2]) * alpha);
+            tmem_st32(tl + o_col + c, u);
+          }
+          tmem_st_wait();
+        }
+        tc_fence_before();
+        FA_TRACE_EV(rnd == 0 && r == 0, 3, g, t);
+        mbar_arrive(bar(L::kBarPFull + g));
+      }
+      // ---- merge the two partials and write O / LSE --------------------------------------
+      if (ok && n_t > 0) {  // committed once per item, after the group's last PV
+        ok = __all_sync(0xffffffffu, wait_bounded(bar(L::kBarPVDone + g),
+                                                  static_cast<uint32_t>(pvc) & 1u, w, kStODone));
+        ++pvc;
       }
       tc_fence_before();
-      mbar_arrive(bar(L::kBarPFull + g));
-    }
-    // ---- merge the two partials and write O / LSE ------------------------------------------
-    if (ok && n_t > 0) {  // committed once, after the warpgroup's last PV
-      ok = __all_sync(0xffffffffu, wait_bounded(bar(L::kBarPVDone + g), 0u, w, kStODone));
-    }
-    tc_fence_before();
-    // Barrier 1: both warpgroups' last PVs are complete, hence every MMA of the CTA is (the last
-    // one issued is one of the two), so the Q tile is free for the exchange.
-    named_barrier_sync(kMergeBarrier, 256);
-    float* xch = reinterpret_cast<float*>(smem + L::kQOff);
-    const bool live = (*abort_flag == 0);
-    if (live) {
+      // Both groups reach both named barriers once per item, on the abort path too; whether to
+      // merge and go on is decided by one thread and read by all after the second barrier.
+      named_barrier_sync(kMergeBarrier, 2 * kBlockM);
       xch[(g * 2 + 0) * kBlockM + r] = m_ref;
       xch[(g * 2 + 1) * kBlockM + r] = l_sum;
-    }
-    named_barrier_sync(kMergeBarrier, 256);
-    if (live && *abort_flag == 0) {
+      if (g == 0 && r == 0) *xch_ctl = *abort_flag;
+      named_barrier_sync(kMergeBarrier, 2 * kBlockM);
+      if (*xch_ctl != 0) break;
       tc_fence_after();
       const float m0 = xch[0 * kBlockM + r], l0 = xch[1 * kBlockM + r];
       const float m1 = xch[2 * kBlockM + r], l1 = xch[3 * kBlockM + r];
@@ -552,34 +660,39 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float f0 = a0 * inv_l, f1 = a1 * inv_l;
       const bool in_range = row < args.N;
       T* orow = reinterpret_cast<T*>(args.o) +
-                (static_cast<size_t>(bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)) * D;
-      // Each warpgroup normalises and stores half of the head dimension.
+                (static_cast<size_t>(item.bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)) * D;
+      // Each group normalises and stores half of the head dimension.
 #pragma unroll
       for (int c = g * (D / 2); c < (g + 1) * (D / 2); c += 32) {
         uint32_t u0[32];
         tmem_ld32_wait(tl + L::kColO + c, u0);
         float o[32];
 #pragma unroll
-        for (int i = 0; i < 32; ++i) o[i] = __uint_as_float(u0[i]) * f0;
+        for (int k2 = 0; k2 < 32; ++k2) o[k2] = __uint_as_float(u0[k2]) * f0;
         if (n_t1 > 0) {
           uint32_t u1[32];
           tmem_ld32_wait(tl + L::kColO + D + c, u1);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = fmaf(__uint_as_float(u1[i]), f1, o[i]);
+          for (int k2 = 0; k2 < 32; ++k2) o[k2] = fmaf(__uint_as_float(u1[k2]), f1, o[k2]);
         }
         uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) pk[i] = pack2<T>(o[2 * i], o[2 * i + 1]);
+        for (int k2 = 0; k2 < 16; ++k2) pk[k2] = pack2<T>(o[2 * k2], o[2 * k2 + 1]);
         if (in_range) {
           uint4* dst = reinterpret_cast<uint4*>(orow + c);
 #pragma unroll
-          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+          for (int k2 = 0; k2 < 4; ++k2) {
+            dst[k2] = make_uint4(pk[4 * k2], pk[4 * k2 + 1], pk[4 * k2 + 2], pk[4 * k2 + 3]);
+          }
         }
       }
       if (g == 0 && in_range) {
-        args.lse[static_cast<size_t>(bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)] =
+        args.lse[static_cast<size_t>(item.bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)] =
             (l > 0.f && m != -INFINITY) ? fmaf(m, args.scale, logf(l)) : INFINITY;
       }
+      // O_0 and O_1 have been read: the next item's first PVs may overwrite them.
+      tc_fence_before();
+      mbar_arrive(bar(L::kBarOFree));
     }
   }
 
@@ -635,10 +748,23 @@ cudaError_t make_tmap(CUtensorMap* m, const void* base, CUtensorMapDataType dt, 
 
 std::atomic<unsigned int> g_epoch_host{0};
 
-template <typename T, int D, int BN, int STAGES, bool CAUSAL>
+int sm_count_of(int dev) {
+  static std::atomic<int> cache[64];
+  const int d = dev & 63;
+  int n = cache[d].load(std::memory_order_relaxed);
+  if (n <= 0) {
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) {
+      n = 148;
+    }
+    cache[d].store(n, std::memory_order_relaxed);
+  }
+  return n;
+}
+
+template <typename T, int D, int BN, int KST, int VST, bool CAUSAL>
 cudaError_t launch_impl(const LaunchArgs& a, cudaStream_t stream) {
-  using L = Layout<D, BN, STAGES>;
-  auto* kern = &fa_fwd_sm100_kernel<T, D, BN, STAGES, CAUSAL>;
+  using L = Layout<D, BN, KST, VST>;
+  auto* kern = &fa_fwd_sm100_kernel<T, D, BN, KST, VST, CAUSAL>;
   static std::atomic<unsigned long long> configured{0};
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
@@ -666,7 +792,12 @@ cudaError_t launch_impl(const LaunchArgs& a, cudaStream_t stream) {
   ka.Hkv = a.Hkv;
   ka.N = a.N;
   ka.n_q_tiles = (a.N + kBlockM - 1) / kBlockM;
-  // K+V of all kv heads: keep head-interleaved order while it fits comfortably in L2.
+  const long long items = hq * ka.n_q_tiles;
+  if (hq > INT_MAX || items <= 0 || items > INT_MAX) return cudaErrorInvalidValue;
+  ka.n_bh = static_cast<int>(hq);
+  ka.n_items = static_cast<int>(items);
+  // K+V of all kv heads: interleave the heads while they fit comfortably in L2, else walk the
+  // query tiles head by head so the CTAs running at once share one head's K/V.
   const double kv_bytes = 2.0 * static_cast<double>(hkv) * a.N * D * 2.0;
   ka.head_major = kv_bytes > 48.0 * 1024 * 1024 ? 1 : 0;
   ka.scale = a.scale;
@@ -676,24 +807,28 @@ cudaError_t launch_impl(const LaunchArgs& a, cudaStream_t stream) {
   if (ep == 0) ep = g_epoch_host.fetch_add(1) + 1;
   ka.epoch = ep;
   ka.skip_kv_tile = a.skip_kv_tile;
-  const long long grid = hq * ka.n_q_tiles;
-  if (grid <= 0 || grid > INT_MAX) return cudaErrorInvalidValue;
-  kern<<<static_cast<unsigned int>(grid), kThreads, L::kSmemAlloc, stream>>>(mq, mk, mv, ka);
+  // Persistent grid: one CTA per SM (the kernel needs a whole SM's TMEM and shared memory).
+  const int grid = static_cast<int>(items < sm_count_of(dev) ? items : sm_count_of(dev));
+  kern<<<grid, kThreads, L::kSmemAlloc, stream>>>(mq, mk, mv, ka);
   return cudaGetLastError();
 }
 
 template <typename T, int D>
 cudaError_t launch_d(const LaunchArgs& a, cudaStream_t s) {
-  // STAGES per key-tile width: as deep as shared memory allows with one CTA per SM.
-  constexpr int kStages128 = (D == 128) ? 3 : 4;
+  // Ring depths per key-tile width: as deep as shared memory allows with one CTA per SM
+  // (D=128, BN=128: 3 K slots + 2 V slots of 32 KB next to the 32 KB Q tile).
+  constexpr int kKSt128 = (D == 128) ? 3 : 4;
+  constexpr int kVSt128 = (D == 128) ? 2 : 4;
   switch (a.block_n) {
     case 128:
-      return a.causal ? launch_impl<T, D, 128, kStages128, true>(a, s)
-                      : launch_impl<T, D, 128, kStages128, false>(a, s);
+      return a.causal ? launch_impl<T, D, 128, kKSt128, kVSt128, true>(a, s)
+                      : launch_impl<T, D, 128, kKSt128, kVSt128, false>(a, s);
     case 64:
-      return a.causal ? launch_impl<T, D, 64, 4, true>(a, s) : launch_impl<T, D, 64, 4, false>(a, s);
+      return a.causal ? launch_impl<T, D, 64, 4, 4, true>(a, s)
+                      : launch_impl<T, D, 64, 4, 4, false>(a, s);
     case 32:
-      return a.causal ? launch_impl<T, D, 32, 4, true>(a, s) : launch_impl<T, D, 32, 4, false>(a, s);
+      return a.causal ? launch_impl<T, D, 32, 4, 4, true>(a, s)
+                      : launch_impl<T, D, 32, 4, 4, false>(a, s);
     default:
       return cudaErrorInvalidValue;
   }
@@ -731,6 +866,15 @@ cudaError_t launch_forward(const LaunchArgs& a, cudaStream_t stream) {
       return cudaErrorNotSupported;
   }
 }
+
+#ifdef FA_TRACE
+extern "C" int fa_debug_read_trace(long long* out, long long* t0) {
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(out, g_trace, sizeof(g_trace));
+  if (e == cudaSuccess) e = cudaMemcpyFromSymbol(t0, g_trace_t0, sizeof(g_trace_t0));
+  return static_cast<int>(e);
+}
+#endif
 
 cudaError_t read_and_clear_status(unsigned int* bits) {
   cudaError_t e = cudaDeviceSynchronize();
