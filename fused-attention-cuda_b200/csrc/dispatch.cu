@@ -2,8 +2,9 @@
 //
 // Reference counterpart: src/dispatch.cu (the fa::forward registry, contract gate, validation
 // and FA_FORCE_BR/BC overrides).  This build has exactly one implementation -- the sm_100a
-// tcgen05 kernel in fa_fwd_sm100.cu, registered as Impl::Tuned -- so the registry collapses to a
-// single gate; there is no fallback and no other backend.  Validation order, error codes and the
+// tcgen05 kernel in fa_fwd_sm100.cu, registered as Impl::Tuned (fp16/bf16) and Impl::Fused
+// (fp32 on tf32, and fp16) -- so the registry collapses to a single gate; there is no fallback
+// and no other backend.  Validation order, error codes and the
 // FA_VERBOSE convention follow the reference (src/dispatch.cu:96-161,
 // src/stage5_tuned.cu:977-1037).
 #include <cmath>
@@ -121,14 +122,31 @@ const char* fa_impl_name(int impl) {
 }
 
 // The kernel is compiled for sm_100a only (the 'a' target runs on compute capability 10.0).
+// Support matrix per stage as in the reference (src/dispatch.cu:76-89): Tuned takes fp16/bf16,
+// Fused takes fp32/fp16.  Both run the one tcgen05 kernel (fp32 on the tf32 tensor-core path);
+// the naive/tiled/wmma teaching stages are not built.
 int fa_impl_supports(int impl, int dtype, int D, int sm) {
-  if (impl != FA_IMPL_TUNED) return 0;
   if (D != 64 && D != 128) return 0;
   if (sm != 100) return 0;
+  switch (impl) {
+    case FA_IMPL_TUNED:
+      if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return 0;
+      break;
+    case FA_IMPL_FUSED:
+      if (dtype != FA_DTYPE_F32 && dtype != FA_DTYPE_F16) return 0;
+      break;
+    default:
+      return 0;
+  }
   return fa_sm100::block_n_supported(dtype, D, fa_sm100::default_block_n(dtype, D, 0)) ? 1 : 0;
 }
 
-size_t fa_workspace_bytes(int /*impl*/, int /*dtype*/, const fa_params_t* /*p*/) { return 0; }
+// 0 for fp16/bf16.  fp32 (Impl::Fused) stages tf32-rounded copies of q, k, v in the workspace.
+size_t fa_workspace_bytes(int impl, int dtype, const fa_params_t* p) {
+  if (p == nullptr || impl != FA_IMPL_FUSED || dtype != FA_DTYPE_F32) return 0;
+  if (p->B <= 0 || p->H <= 0 || p->Hkv <= 0 || p->N <= 0 || p->D <= 0) return 0;
+  return fa_sm100::workspace_bytes_f32(p->B, p->H, p->Hkv, p->N, p->D);
+}
 
 void fa_set_debug_overrides(int block_m, int block_n) {
   g_block_m = block_m;
@@ -154,8 +172,7 @@ int fa_last_device_error(unsigned int* detail) {
 }
 
 int fa_forward(int impl, int dtype, const void* q, const void* k, const void* v, void* o,
-               float* lse, void* /*workspace: the fused kernel needs none*/,
-               const fa_params_t* p, cudaStream_t stream) {
+               float* lse, void* workspace, const fa_params_t* p, cudaStream_t stream) {
   if (const char* why = validate(dtype, q, k, v, o, lse, p)) {
     if (verbose()) std::fprintf(stderr, "fa_forward: invalid params: %s\n", why);
     return cudaErrorInvalidValue;
@@ -168,6 +185,13 @@ int fa_forward(int impl, int dtype, const void* q, const void* k, const void* v,
                    fa_impl_name(impl), fa_dtype_name(dtype), p->D, sm);
     }
     return cudaErrorNotSupported;
+  }
+  if (fa_workspace_bytes(impl, dtype, p) > 0 && (workspace == nullptr || !aligned16(workspace))) {
+    if (verbose()) {
+      std::fprintf(stderr, "fa_forward: workspace must be non-null and 16-byte aligned "
+                           "(fa_workspace_bytes > 0)\n");
+    }
+    return cudaErrorInvalidValue;
   }
   int bm = 0, bn = 0;
   fa_get_debug_overrides(1, &bm, &bn);
@@ -199,6 +223,7 @@ int fa_forward(int impl, int dtype, const void* q, const void* k, const void* v,
   a.block_n = bn;
   a.timeout_ns = g_timeout_ns;
   a.skip_kv_tile = g_skip_kv_tile;
+  a.workspace = workspace;
   return static_cast<int>(fa_sm100::launch_forward(a, stream));
 }
 

@@ -97,9 +97,9 @@ constexpr int kSoftmaxWarp0 = 4;  // warps 4..11: two softmax warpgroups
 constexpr int kMergeBarrier = 1;  // named barrier id shared by the 256 softmax threads
 constexpr float kRescaleThreshold = 8.0f;
 
-template <int D, int BN, int KST, int VST>
+template <int EB, int D, int BN, int KST, int VST>
 struct Layout {
-  static constexpr int kEB = 2;                  // bytes per element (fp16/bf16)
+  static constexpr int kEB = EB;                 // bytes per element (2: fp16/bf16, 4: fp32)
   static constexpr int kSwElems = 128 / kEB;     // elements per 128-byte swizzle row
   static constexpr int kDChunks = D / kSwElems;  // 128-byte column chunks along D
   static constexpr int kQChunkBytes = kBlockM * 128;
@@ -139,6 +139,11 @@ struct Layout {
   static constexpr int kBarKEmpty = 10 + KST;            // + stage
   static constexpr int kBarVFull = 10 + 2 * KST;         // + stage
   static constexpr int kBarVEmpty = 10 + 2 * KST + VST;  // + stage
+
+  // tcgen05.mma steps: 32 bytes of K per instruction (16 fp16/bf16 or 8 tf32 elements).
+  static constexpr int kSSteps = D * EB / 32;     // S = Q K^T: K dimension = D
+  static constexpr int kPVSteps = BN * EB / 32;   // O += P V: K dimension = BN keys
+  static constexpr int kPVStepBytes = (32 / EB) * 128;  // V rows consumed per step x 128 B
 
   static_assert(D % kSwElems == 0, "D must be a multiple of the swizzle width");
   static_assert(BN % 32 == 0 && BN >= 32 && BN <= 128, "BN must be 32, 64 or 128");
@@ -310,6 +315,33 @@ __device__ __forceinline__ float exp_pack_store(const float (&s)[BN], float sl2,
   return f2_lo(t) + f2_hi(t);
 }
 
+// fp32 flavour for the tf32 path: p = 2^(s*c - m*c) for all BN columns, stored one weight per
+// TMEM column (rounded to tf32, the precision the tensor core multiplies) over S_g itself.
+// Returns the sum of the unrounded weights.
+template <int BN>
+__device__ __forceinline__ float exp_store_f32(const float (&s)[BN], float sl2, float mc,
+                                               uint32_t taddr) {
+  const uint64_t c2 = f2_pack(sl2, sl2);
+  const uint64_t nb2 = f2_pack(-mc, -mc);
+  uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll
+  for (int c0 = 0; c0 < BN; c0 += 32) {
+    uint32_t w32[32];
+#pragma unroll
+    for (int c = 0; c < 32; c += 2) {
+      const uint64_t x = f2_fma(f2_pack(s[c0 + c], s[c0 + c + 1]), c2, nb2);
+      const float p0 = ex2_approx(f2_lo(x));
+      const float p1 = ex2_approx(f2_hi(x));
+      w32[c] = f32_to_tf32(p0);
+      w32[c + 1] = f32_to_tf32(p1);
+      acc[(c >> 1) & 3] = f2_add(acc[(c >> 1) & 3], f2_pack(p0, p1));
+    }
+    tmem_st32(taddr + c0, w32);
+  }
+  const uint64_t t = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
+  return f2_lo(t) + f2_hi(t);
+}
+
 __device__ __forceinline__ void named_barrier_sync(int id, int threads) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
 }
@@ -319,8 +351,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
                         const __grid_constant__ CUtensorMap tm_v, const KArgs args) {
-  using L = Layout<D, BN, KST, VST>;
-  constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : 0u;
+  using L = Layout<static_cast<int>(sizeof(T)), D, BN, KST, VST>;
+  constexpr bool kTf32 = std::is_same<T, float>::value;
+  constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : (kTf32 ? 2u : 0u);
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -450,7 +483,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // stays below 2^14 in 16-byte units for any shared-memory address, so it cannot carry).
       const uint64_t q_desc0 = sdesc_sw128(sbase + L::kQOff, 16, 1024);
       const uint64_t k_desc0 = sdesc_sw128(sbase + L::kKOff, 16, 1024);
-      const uint64_t v_desc0 = sdesc_sw128(sbase + L::kVOff, L::kKVChunkBytes, 1024);
+      // V is the MN-major B operand (D contiguous).  16-bit: 128-byte swizzle, 8-row K groups;
+      // tf32: 128-byte swizzle with 32-byte atoms, 4-row K groups.
+      const uint64_t v_desc0 = kTf32 ? sdesc_sw128_atom32(sbase + L::kVOff, L::kKVChunkBytes, 512)
+                                     : sdesc_sw128(sbase + L::kVOff, L::kKVChunkBytes, 1024);
       int kc = 0, vc = 0;   // K / V tiles consumed, over all items
       int pc[2] = {0, 0};   // P tiles consumed per group, over all items
       int it = 0;           // items processed
@@ -477,11 +513,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t d_tmem = tmem + L::kColS + g * BN;
           const uint64_t k_desc = k_desc0 + static_cast<uint64_t>((s * L::kKVBytes) >> 4);
 #pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
+          for (int kk = 0; kk < L::kSSteps; ++kk) {
             const uint32_t q_off = (kk / 4) * L::kQChunkBytes + (kk % 4) * 32;
             const uint32_t k_off = (kk / 4) * L::kKVChunkBytes + (kk % 4) * 32;
-            umma_ss(d_tmem, q_desc0 + (q_off >> 4), k_desc + (k_off >> 4), kIdescS,
-                    kk > 0 ? 1u : 0u);
+            if constexpr (kTf32) {
+              umma_ss_tf32(d_tmem, q_desc0 + (q_off >> 4), k_desc + (k_off >> 4), kIdescS,
+                           kk > 0 ? 1u : 0u);
+            } else {
+              umma_ss(d_tmem, q_desc0 + (q_off >> 4), k_desc + (k_off >> 4), kIdescS,
+                      kk > 0 ? 1u : 0u);
+            }
           }
           umma_commit(bar(L::kBarSFull + g));
           umma_commit(bar(L::kBarKEmpty + s));
@@ -506,15 +547,23 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint64_t v_desc = v_desc0 + static_cast<uint64_t>((s * L::kKVBytes) >> 4);
           const uint32_t pa = tmem + L::kColS + g * BN;
           const uint32_t o_tmem = tmem + L::kColO + g * D;
+          // Each step reads 8 TMEM columns of P (16 packed 16-bit weights or 8 fp32 ones).
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            umma_ts(o_tmem, pa + kk * 8, v_desc + ((kk * 16 * 128) >> 4), kIdescPV,
-                    (t > 0 || kk > 0) ? 1u : 0u);
+          for (int kk = 0; kk < L::kPVSteps; ++kk) {
+            const uint64_t vd = v_desc + ((kk * L::kPVStepBytes) >> 4);
+            if constexpr (kTf32) {
+              umma_ts_tf32(o_tmem, pa + kk * 8, vd, kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
+            } else {
+              umma_ts(o_tmem, pa + kk * 8, vd, kIdescPV, (t > 0 || kk > 0) ? 1u : 0u);
+            }
           }
-          if (comp) {
+          if constexpr (!kTf32) {
+            if (comp) {
 #pragma unroll
-            for (int kk = 0; kk < BN / 16; ++kk) {
-              umma_ts(o_tmem, pa + BN / 2 + kk * 8, v_desc + ((kk * 16 * 128) >> 4), kIdescPV, 1u);
+              for (int kk = 0; kk < L::kPVSteps; ++kk) {
+                umma_ts(o_tmem, pa + BN / 2 + kk * 8, v_desc + ((kk * L::kPVStepBytes) >> 4),
+                        kIdescPV, 1u);
+              }
             }
           }
           if (last) umma_commit(bar(L::kBarPVDone + g));
@@ -608,7 +657,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         FA_TRACE_EV(rnd == 0 && r == 0, 5, g, t);
         // P_g over the first half of S_g (all of S_g's row is in registers by now).
         float rs;
-        if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        if constexpr (kTf32) {
+          rs = exp_store_f32<BN>(s, sl2, mc, tl + s_col);
+        } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
           rs = comp ? exp_pack_store<T, BN, 0, BN / 2, true>(s, sl2, mc, tl + s_col)
                     : exp_pack_store<T, BN, 0, BN / 2, false>(s, sl2, mc, tl + s_col);
         } else {
@@ -675,14 +726,24 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k2 = 0; k2 < 32; ++k2) o[k2] = fmaf(__uint_as_float(u1[k2]), f1, o[k2]);
         }
-        uint32_t pk[16];
+        if constexpr (kTf32) {
+          if (in_range) {
+            float4* dst = reinterpret_cast<float4*>(orow + c);
 #pragma unroll
-        for (int k2 = 0; k2 < 16; ++k2) pk[k2] = pack2<T>(o[2 * k2], o[2 * k2 + 1]);
-        if (in_range) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c);
+            for (int k2 = 0; k2 < 8; ++k2) {
+              dst[k2] = make_float4(o[4 * k2], o[4 * k2 + 1], o[4 * k2 + 2], o[4 * k2 + 3]);
+            }
+          }
+        } else {
+          uint32_t pk[16];
 #pragma unroll
-          for (int k2 = 0; k2 < 4; ++k2) {
-            dst[k2] = make_uint4(pk[4 * k2], pk[4 * k2 + 1], pk[4 * k2 + 2], pk[4 * k2 + 3]);
+          for (int k2 = 0; k2 < 16; ++k2) pk[k2] = pack2<T>(o[2 * k2], o[2 * k2 + 1]);
+          if (in_range) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + c);
+#pragma unroll
+            for (int k2 = 0; k2 < 4; ++k2) {
+              dst[k2] = make_uint4(pk[4 * k2], pk[4 * k2 + 1], pk[4 * k2 + 2], pk[4 * k2 + 3]);
+            }
           }
         }
       }
@@ -702,6 +763,23 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, L::kTmemCols);
+  }
+}
+
+// fp32 inputs would enter the tf32 tensor core with their low 13 mantissa bits dropped
+// (truncation: a bias toward zero that shifts every score the same way).  The fp32 path first
+// rounds q, k and v to tf32 (round to nearest, ties away) into the caller's workspace, laid out
+// [q | k | v], so the products carry unbiased rounding errors.  HBM-bound: 16 bytes in and out
+// per thread and step, grid-stride.
+__global__ void __launch_bounds__(256)
+    fa_round_tf32_kernel(const uint4* __restrict__ q, size_t nq, const uint4* __restrict__ k,
+                         size_t nk, const uint4* __restrict__ v, size_t nv, uint4* __restrict__ out) {
+  const size_t n = nq + nk + nv;
+  const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
+  for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
+    const uint4 x = i < nq ? q[i] : (i < nq + nk ? k[i - nq] : v[i - nq - nk]);
+    out[i] = make_uint4(f32_to_tf32(__uint_as_float(x.x)), f32_to_tf32(__uint_as_float(x.y)),
+                        f32_to_tf32(__uint_as_float(x.z)), f32_to_tf32(__uint_as_float(x.w)));
   }
 }
 
@@ -730,7 +808,8 @@ EncodeTiledFn get_encode_fn() {
 // [heads, N, D] view of a contiguous [B, H, N, D] tensor; box = 128 bytes of D x `rows` rows.
 // Rows past N (inside one head) are zero-filled by the TMA unit.
 cudaError_t make_tmap(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes,
-                      int D, int N, long long heads, int rows) {
+                      int D, int N, long long heads, int rows,
+                      CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   const EncodeTiledFn enc = get_encode_fn();
   if (enc == nullptr) return cudaErrorNotSupported;
   const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(N),
@@ -741,7 +820,7 @@ cudaError_t make_tmap(CUtensorMap* m, const void* base, CUtensorMapDataType dt, 
                              static_cast<cuuint32_t>(rows), 1u};
   const cuuint32_t estride[3] = {1u, 1u, 1u};
   const CUresult r = enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estride,
-                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
@@ -763,7 +842,8 @@ int sm_count_of(int dev) {
 
 template <typename T, int D, int BN, int KST, int VST, bool CAUSAL>
 cudaError_t launch_impl(const LaunchArgs& a, cudaStream_t stream) {
-  using L = Layout<D, BN, KST, VST>;
+  constexpr int kEB = static_cast<int>(sizeof(T));
+  using L = Layout<kEB, D, BN, KST, VST>;
   auto* kern = &fa_fwd_sm100_kernel<T, D, BN, KST, VST, CAUSAL>;
   static std::atomic<unsigned long long> configured{0};
   int dev = 0;
@@ -777,13 +857,17 @@ cudaError_t launch_impl(const LaunchArgs& a, cudaStream_t stream) {
   }
   const CUtensorMapDataType dt = std::is_same<T, __nv_bfloat16>::value
                                      ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
-                                     : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+                                 : std::is_same<T, float>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
+                                                                 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   alignas(64) CUtensorMap mq, mk, mv;
   const long long hq = static_cast<long long>(a.B) * a.H;
   const long long hkv = static_cast<long long>(a.B) * a.Hkv;
-  if ((e = make_tmap(&mq, a.q, dt, 2, D, a.N, hq, kBlockM)) != cudaSuccess) return e;
-  if ((e = make_tmap(&mk, a.k, dt, 2, D, a.N, hkv, BN)) != cudaSuccess) return e;
-  if ((e = make_tmap(&mv, a.v, dt, 2, D, a.N, hkv, BN)) != cudaSuccess) return e;
+  if ((e = make_tmap(&mq, a.q, dt, kEB, D, a.N, hq, kBlockM)) != cudaSuccess) return e;
+  if ((e = make_tmap(&mk, a.k, dt, kEB, D, a.N, hkv, BN)) != cudaSuccess) return e;
+  // tf32 V is an MN-major operand: 32-byte swizzle atoms (see sdesc_sw128_atom32).
+  const CUtensorMapSwizzle v_swizzle =
+      kEB == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
+  if ((e = make_tmap(&mv, a.v, dt, kEB, D, a.N, hkv, BN, v_swizzle)) != cudaSuccess) return e;
 
   KArgs ka;
   ka.o = a.o;
@@ -798,7 +882,7 @@ cudaError_t launch_impl(const LaunchArgs& a, cudaStream_t stream) {
   ka.n_items = static_cast<int>(items);
   // K+V of all kv heads: interleave the heads while they fit comfortably in L2, else walk the
   // query tiles head by head so the CTAs running at once share one head's K/V.
-  const double kv_bytes = 2.0 * static_cast<double>(hkv) * a.N * D * 2.0;
+  const double kv_bytes = 2.0 * static_cast<double>(hkv) * a.N * D * kEB;
   ka.head_major = kv_bytes > 48.0 * 1024 * 1024 ? 1 : 0;
   ka.scale = a.scale;
   ka.scale_log2 = a.scale * 1.4426950408889634f;
@@ -813,26 +897,55 @@ cudaError_t launch_impl(const LaunchArgs& a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// Ring depth for one key-tile width: as many K and V slots (up to 4 each) as fit next to the Q
+// tile in ~200 KB of shared memory with one CTA per SM.
+constexpr int ring_depth(int eb, int d, int bn) {
+  return ((200 * 1024 - 128 * d * eb) / (2 * bn * d * eb)) < 4
+             ? ((200 * 1024 - 128 * d * eb) / (2 * bn * d * eb))
+             : 4;
+}
+
+template <typename T, int D, int BN, int KST, int VST>
+cudaError_t launch_c(const LaunchArgs& a, cudaStream_t s) {
+  return a.causal ? launch_impl<T, D, BN, KST, VST, true>(a, s)
+                  : launch_impl<T, D, BN, KST, VST, false>(a, s);
+}
+
 template <typename T, int D>
 cudaError_t launch_d(const LaunchArgs& a, cudaStream_t s) {
-  // Ring depths per key-tile width: as deep as shared memory allows with one CTA per SM
-  // (D=128, BN=128: 3 K slots + 2 V slots of 32 KB next to the 32 KB Q tile).
-  constexpr int kKSt128 = (D == 128) ? 3 : 4;
-  constexpr int kVSt128 = (D == 128) ? 2 : 4;
-  switch (a.block_n) {
-    case 128:
-      return a.causal ? launch_impl<T, D, 128, kKSt128, kVSt128, true>(a, s)
-                      : launch_impl<T, D, 128, kKSt128, kVSt128, false>(a, s);
-    case 64:
-      return a.causal ? launch_impl<T, D, 64, 4, 4, true>(a, s)
-                      : launch_impl<T, D, 64, 4, 4, false>(a, s);
-    case 32:
-      return a.causal ? launch_impl<T, D, 32, 4, 4, true>(a, s)
-                      : launch_impl<T, D, 32, 4, 4, false>(a, s);
-    default:
-      return cudaErrorInvalidValue;
+  constexpr int kEB = static_cast<int>(sizeof(T));
+  if constexpr (kEB == 4) {
+    // fp32 on tf32: 32- and 64-key tiles (and 128 at D=64), symmetric rings.
+    switch (a.block_n) {
+      case 64:
+        return launch_c<T, D, 64, ring_depth(4, D, 64), ring_depth(4, D, 64)>(a, s);
+      case 32:
+        return launch_c<T, D, 32, ring_depth(4, D, 32), ring_depth(4, D, 32)>(a, s);
+      case 128:
+        if constexpr (D == 64) return launch_c<T, D, 128, 2, 2>(a, s);
+        return cudaErrorInvalidValue;
+      default:
+        return cudaErrorInvalidValue;
+    }
+  } else {
+    // D=128, BN=128: 3 K slots + 2 V slots of 32 KB next to the 32 KB Q tile.
+    constexpr int kKSt128 = (D == 128) ? 3 : 4;
+    constexpr int kVSt128 = (D == 128) ? 2 : 4;
+    switch (a.block_n) {
+      case 128:
+        return launch_c<T, D, 128, kKSt128, kVSt128>(a, s);
+      case 64:
+        return launch_c<T, D, 64, 4, 4>(a, s);
+      case 32:
+        return launch_c<T, D, 32, 4, 4>(a, s);
+      default:
+        return cudaErrorInvalidValue;
+    }
   }
 }
+
+// fp32: round q/k/v into the workspace, then run the tf32 kernel on the rounded copies.
+cudaError_t launch_f32(const LaunchArgs& a, cudaStream_t s);
 
 template <typename T>
 cudaError_t launch_t(const LaunchArgs& a, cudaStream_t s) {
@@ -850,11 +963,12 @@ cudaError_t launch_t(const LaunchArgs& a, cudaStream_t s) {
 
 bool block_n_supported(int dtype, int D, int block_n) {
   if (D != 64 && D != 128) return false;
+  if (dtype == FA_DTYPE_F32) return block_n == 32 || block_n == 64 || (block_n == 128 && D == 64);
   if (dtype != FA_DTYPE_F16 && dtype != FA_DTYPE_BF16) return false;
   return block_n == 32 || block_n == 64 || block_n == 128;
 }
 
-int default_block_n(int /*dtype*/, int /*D*/, int /*N*/) { return 128; }
+int default_block_n(int dtype, int /*D*/, int /*N*/) { return dtype == FA_DTYPE_F32 ? 64 : 128; }
 
 cudaError_t launch_forward(const LaunchArgs& a, cudaStream_t stream) {
   switch (a.dtype) {
@@ -862,9 +976,41 @@ cudaError_t launch_forward(const LaunchArgs& a, cudaStream_t stream) {
       return launch_t<__half>(a, stream);
     case FA_DTYPE_BF16:
       return launch_t<__nv_bfloat16>(a, stream);
+    case FA_DTYPE_F32:
+      return launch_f32(a, stream);
     default:
       return cudaErrorNotSupported;
   }
+}
+
+namespace {
+cudaError_t launch_f32(const LaunchArgs& a, cudaStream_t s) {
+  if (a.workspace == nullptr) return cudaErrorInvalidValue;
+  const size_t nq = static_cast<size_t>(a.B) * a.H * a.N * a.D / 4;  // 16-byte units
+  const size_t nkv = static_cast<size_t>(a.B) * a.Hkv * a.N * a.D / 4;
+  uint4* ws = static_cast<uint4*>(a.workspace);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  const size_t n = nq + 2 * nkv;
+  const size_t want = (n + 255) / 256;
+  const size_t cap = static_cast<size_t>(sm_count_of(dev)) * 8;
+  const unsigned int grid = static_cast<unsigned int>(want < cap ? want : cap);
+  fa_round_tf32_kernel<<<grid, 256, 0, s>>>(static_cast<const uint4*>(a.q), nq,
+                                             static_cast<const uint4*>(a.k), nkv,
+                                             static_cast<const uint4*>(a.v), nkv, ws);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  LaunchArgs r = a;
+  r.q = ws;
+  r.k = ws + nq;
+  r.v = ws + nq + nkv;
+  return launch_t<float>(r, s);
+}
+}  // namespace
+
+size_t workspace_bytes_f32(int B, int H, int Hkv, int N, int D) {
+  return 4ull * static_cast<size_t>(D) * static_cast<size_t>(N) *
+         (static_cast<size_t>(B) * H + 2ull * static_cast<size_t>(B) * Hkv);
 }
 
 #ifdef FA_TRACE

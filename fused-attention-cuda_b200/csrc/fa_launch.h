@@ -21,11 +21,15 @@ struct LaunchArgs {
   int block_n;  // keys per tile: 32, 64 or 128
   unsigned long long timeout_ns;
   int skip_kv_tile;  // fault injection, -1 = off
+  void* workspace;   // fp32 only: tf32-rounded q|k|v, workspace_bytes_f32() bytes
 };
 
 // Which key-tile widths this build instantiates for (dtype, D).
 bool block_n_supported(int dtype, int D, int block_n);
 int default_block_n(int dtype, int D, int N);
+
+// Workspace of the fp32 path: tf32-rounded copies of q, k and v.
+size_t workspace_bytes_f32(int B, int H, int Hkv, int N, int D);
 
 // Validated arguments only; returns the launch status (never synchronises).
 cudaError_t launch_forward(const LaunchArgs& a, cudaStream_t stream);

@@ -304,6 +304,16 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo, ui
          (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (2ull << 61);
 }
 
+// MN-major 32-bit (tf32) operand: 128-byte swizzle with 32-byte atoms (layout type 1), the only
+// MN-major layout tcgen05.mma accepts for tf32.  Rows of 128 bytes; `lbo` = distance between
+// 128-byte-wide MN chunks, `sbo` = distance between 4-row K groups (512 for dense rows).  The
+// matching TMA swizzle mode is CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B.
+__device__ __forceinline__ uint64_t sdesc_sw128_atom32(uint32_t saddr, uint32_t lbo, uint32_t sbo) {
+  return static_cast<uint64_t>((saddr & 0x3FFFFu) >> 4) |
+         (static_cast<uint64_t>((lbo >> 4) & 0x3FFFu) << 16) |
+         (static_cast<uint64_t>((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | (1ull << 61);
+}
+
 // fmt: 0 = f16, 1 = bf16, 2 = tf32.  D is always f32.
 __host__ __device__ constexpr uint32_t idesc_mma(uint32_t fmt, int M, int N, bool b_mn_major) {
   return (1u << 4) | (fmt << 7) | (fmt << 10) | ((b_mn_major ? 1u : 0u) << 16) |
@@ -335,6 +345,14 @@ __device__ __forceinline__ float ex2_poly3(float x) {
   p = fmaf(p, f, 0.6932609677314758f);
   p = fmaf(p, f, 0.9999280571937561f);
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+// fp32 -> tf32 bit pattern (round to nearest, ties away from zero; the low 13 mantissa bits
+// cleared), so the tensor core's tf32 operand is the rounded value, not the truncated one.
+__device__ __forceinline__ uint32_t f32_to_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
 }
 
 // Three-input maximum (one instruction on sm_100).

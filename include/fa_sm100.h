@@ -34,8 +34,8 @@ extern "C" {
 enum fa_dtype { FA_DTYPE_F32 = 0, FA_DTYPE_F16 = 1, FA_DTYPE_BF16 = 2 };
 
 /* Implementation id -- fa::Impl (attention.cuh:20-26).  This build implements FA_IMPL_TUNED
- * only, and on B200 it is the tcgen05/TMA kernel; the reference's teaching rungs 1-4 report
- * cudaErrorNotSupported. */
+ * (fp16/bf16) and FA_IMPL_FUSED (fp32 on tf32 tensor cores, and fp16), both on the one
+ * tcgen05/TMA kernel; the reference's teaching rungs 1, 2 and 4 report cudaErrorNotSupported. */
 enum fa_impl {
   FA_IMPL_NAIVE = 1,
   FA_IMPL_TILED = 2,
@@ -56,11 +56,15 @@ typedef struct fa_params {
 } fa_params_t;
 
 /* fa::forward (attention.cuh:46-47; implementation src/dispatch.cu:140-161).
- * Launches the fused forward on `stream`.  `workspace` may be NULL (fa_workspace_bytes is 0). */
+ * Launches the fused forward on `stream`.  `workspace` (caller-owned, 16-byte aligned) must hold
+ * fa_workspace_bytes(impl, dtype, p) bytes; it may be NULL when that is 0.  The kernel reads
+ * q, k, v and writes only o, lse and the workspace. */
 int fa_forward(int impl, int dtype, const void* q, const void* k, const void* v, void* o,
                float* lse, void* workspace, const fa_params_t* p, cudaStream_t stream);
 
-/* fa::workspace_bytes (attention.cuh:51; src/dispatch.cu:163-168).  0 for the fused kernel. */
+/* fa::workspace_bytes (attention.cuh:51; src/dispatch.cu:163-168).  0 for fp16/bf16.  For fp32
+ * (FA_IMPL_FUSED, tf32 tensor cores) 4*D*N*(B*H + 2*B*Hkv) bytes: q, k and v rounded to tf32
+ * (round to nearest) before the kernel reads them, instead of the tensor core's truncation. */
 size_t fa_workspace_bytes(int impl, int dtype, const fa_params_t* p);
 
 /* fa::impl_supports (attention.cuh:56; src/dispatch.cu:170-175).  `sm` = major*10+minor. */

@@ -53,20 +53,35 @@ def test_names_and_sizes_match_reference():
     assert abi.dtype_size(7) == 0 and abi.dtype_name(7) == "unknown"
 
 
-def test_impl_supports_only_tuned_on_sm100():
-    for dt in (abi.FA_DTYPE_F16, abi.FA_DTYPE_BF16):
+def test_impl_supports_matrix_on_sm100():
+    """Stage support as in the reference's contract gate (src/dispatch.cu:76-89), sm_100 only:
+    Tuned takes fp16/bf16, Fused takes fp32 (tf32 tensor cores) and fp16; stages 1, 2, 4 are
+    not built."""
+    want = {
+        abi.FA_IMPL_TUNED: {abi.FA_DTYPE_F16, abi.FA_DTYPE_BF16},
+        abi.FA_IMPL_FUSED: {abi.FA_DTYPE_F32, abi.FA_DTYPE_F16},
+    }
+    for dt in (abi.FA_DTYPE_F32, abi.FA_DTYPE_F16, abi.FA_DTYPE_BF16):
         for d in (64, 128):
-            assert abi.impl_supports(abi.FA_IMPL_TUNED, dt, d, 100)
-            assert not abi.impl_supports(abi.FA_IMPL_TUNED, dt, d, 90)
-            assert not abi.impl_supports(abi.FA_IMPL_TUNED, dt, d, 103)
-            for impl in (1, 2, 3, 4):
-                assert not abi.impl_supports(impl, dt, d, 100)
-        assert not abi.impl_supports(abi.FA_IMPL_TUNED, dt, 96, 100)
+            for impl in (1, 2, 3, 4, 5):
+                ok = dt in want.get(impl, set())
+                assert bool(abi.impl_supports(impl, dt, d, 100)) == ok, (impl, dt, d)
+                assert not abi.impl_supports(impl, dt, d, 90)
+                assert not abi.impl_supports(impl, dt, d, 103)
+            assert not abi.impl_supports(abi.FA_IMPL_TUNED, dt, 96, 100)
+            assert not abi.impl_supports(abi.FA_IMPL_FUSED, dt, 96, 100)
 
 
-def test_workspace_is_zero():
+def test_workspace_bytes():
+    """0 for fp16/bf16 (fused kernel, as the reference's fused stages); fp32 on Impl::Fused
+    stages tf32-rounded q, k, v: 4*D*N*(B*H + 2*B*Hkv) bytes."""
     p = abi.params(2, 8, 8, 2048, 128, 0.088, True)
     assert abi.workspace_bytes(abi.FA_IMPL_TUNED, abi.FA_DTYPE_F16, p) == 0
+    assert abi.workspace_bytes(abi.FA_IMPL_TUNED, abi.FA_DTYPE_BF16, p) == 0
+    assert abi.workspace_bytes(abi.FA_IMPL_FUSED, abi.FA_DTYPE_F16, p) == 0
+    assert abi.workspace_bytes(abi.FA_IMPL_FUSED, abi.FA_DTYPE_F32, p) == 4 * 128 * 2048 * (16 + 32)
+    g = abi.params(2, 8, 2, 256, 64, 0.125, False)
+    assert abi.workspace_bytes(abi.FA_IMPL_FUSED, abi.FA_DTYPE_F32, g) == 4 * 64 * 256 * (16 + 8)
 
 
 def test_debug_overrides_roundtrip_and_env(monkeypatch):

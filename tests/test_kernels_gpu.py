@@ -361,7 +361,7 @@ def test_input_validation_messages(make_qkv):
         fused_attn.forward(qm, k, v)
     with pytest.raises(RuntimeError, match="scale must be finite"):
         fused_attn.forward(q, k, v, scale=0.0)
-    for stage in (1, 2, 3, 4):
+    for stage in (1, 2, 4):
         with pytest.raises(RuntimeError, match="not implemented"):
             fused_attn.forward_stage(q, k, v, stage)
     with pytest.raises(RuntimeError, match="not implemented|no stage"):
