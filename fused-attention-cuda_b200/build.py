@@ -36,7 +36,7 @@ NVCC_FLAGS = [*ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPI
               "-Xcompiler", "-Wall", f"-I{INCLUDE}", f"-I{CSRC}"]
 
 KERNEL_SOURCES = ["fa_fwd_sm100.cu", "dispatch.cu"]
-KERNEL_HEADERS = ["sm100_ptx.cuh", "fa_launch.h"]
+KERNEL_HEADERS = ["sm100_ptx.cuh", "fa_launch.h", "fa_kernel_common.cuh", "fa_fwd_lookahead.cuh"]
 
 LIB_NAME = "libfa_sm100.so"
 EXT_NAME = "_C" + (sysconfig.get_config_var("EXT_SUFFIX") or ".so")

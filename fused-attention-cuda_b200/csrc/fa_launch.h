@@ -47,6 +47,8 @@ enum StatusBits : unsigned int {
   kStODone = 1u << 5,    // softmax warps waiting for an O update
   kStKVEmpty = 1u << 6,  // producer waiting for a free K/V slot
   kStDrain = 1u << 7,    // exit path waiting for in-flight copies / MMAs
+  kStSFree = 1u << 8,    // MMA warp waiting for the softmax warps to read S (lookahead kernel)
+  kStPFree = 1u << 9,    // softmax warps waiting for a PV to release P (lookahead kernel)
 };
 
 }  // namespace fa_sm100

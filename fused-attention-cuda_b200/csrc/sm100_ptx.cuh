@@ -177,6 +177,13 @@ __device__ __forceinline__ void umma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64
       : "memory");
 }
 
+// Copies one 128-row x 256-bit slice of a shared-memory operand (the A slice of one 16-bit K step,
+// described by a matrix descriptor exactly as for tcgen05.mma) into TMEM columns
+// [taddr, taddr + 8) of lanes 0-127.  Asynchronous, one thread issues; tcgen05.commit tracks it.
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t taddr, uint64_t sdesc) {
+  asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(taddr), "l"(sdesc) : "memory");
+}
+
 // tf32 flavour (fp32 operands in memory, 10-bit mantissa inside the tensor core).
 __device__ __forceinline__ void umma_ss_tf32(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
                                              uint32_t idesc, uint32_t accumulate) {
