@@ -171,11 +171,41 @@ int fa_last_device_error(unsigned int* detail) {
   return static_cast<int>(fa_sm100::read_and_clear_status(detail));
 }
 
-int fa_forward(int impl, int dtype, const void* q, const void* k, const void* v, void* o,
-               float* lse, void* workspace, const fa_params_t* p, cudaStream_t stream) {
+}  // extern "C"
+
+namespace {
+
+// Stride rules of a strided view: positive element strides whose byte sizes are multiples of 16
+// (the TMA tensor-map rule; with a 16-byte-aligned base every row then starts 16-byte aligned).
+const char* check_strides(const long long st[3], size_t eb, const char* name) {
+  for (int i = 0; i < 3; ++i) {
+    if (st[i] <= 0) return name;
+    if ((static_cast<unsigned long long>(st[i]) * eb) % 16 != 0) return name;
+    if (static_cast<unsigned long long>(st[i]) * eb >= (1ull << 40)) return name;
+  }
+  return nullptr;
+}
+
+int forward_impl(int impl, int dtype, const void* q, const void* k, const void* v, void* o,
+                 float* lse, void* workspace, const fa_params_t* p, const fa_strides_t* st,
+                 cudaStream_t stream) {
   if (const char* why = validate(dtype, q, k, v, o, lse, p)) {
     if (verbose()) std::fprintf(stderr, "fa_forward: invalid params: %s\n", why);
     return cudaErrorInvalidValue;
+  }
+  if (st != nullptr) {
+    const size_t eb = fa_dtype_size(dtype);
+    const char* bad = check_strides(st->q, eb, "q");
+    if (bad == nullptr) bad = check_strides(st->k, eb, "k");
+    if (bad == nullptr) bad = check_strides(st->v, eb, "v");
+    if (bad == nullptr) bad = check_strides(st->o, eb, "o");
+    if (bad != nullptr) {
+      if (verbose()) {
+        std::fprintf(stderr, "fa_forward_strided: %s strides must be positive multiples of 16 "
+                             "bytes\n", bad);
+      }
+      return cudaErrorInvalidValue;
+    }
   }
   int sm = 0;
   if (const cudaError_t e = current_sm(&sm)) return e;
@@ -224,7 +254,42 @@ int fa_forward(int impl, int dtype, const void* q, const void* k, const void* v,
   a.timeout_ns = g_timeout_ns;
   a.skip_kv_tile = g_skip_kv_tile;
   a.workspace = workspace;
+  if (st != nullptr) {
+    for (int i = 0; i < 3; ++i) {
+      a.sq[i] = st->q[i];
+      a.sk[i] = st->k[i];
+      a.sv[i] = st->v[i];
+      a.so[i] = st->o[i];
+    }
+  } else {
+    // Contiguous [B, H, N, D] (q, o) and [B, Hkv, N, D] (k, v).
+    const long long nd = static_cast<long long>(p->N) * p->D;
+    const long long cq[3] = {static_cast<long long>(p->H) * nd, nd, p->D};
+    const long long ckv[3] = {static_cast<long long>(p->Hkv) * nd, nd, p->D};
+    for (int i = 0; i < 3; ++i) {
+      a.sq[i] = cq[i];
+      a.so[i] = cq[i];
+      a.sk[i] = ckv[i];
+      a.sv[i] = ckv[i];
+    }
+  }
   return static_cast<int>(fa_sm100::launch_forward(a, stream));
+}
+
+}  // namespace
+
+extern "C" {
+
+int fa_forward(int impl, int dtype, const void* q, const void* k, const void* v, void* o,
+               float* lse, void* workspace, const fa_params_t* p, cudaStream_t stream) {
+  return forward_impl(impl, dtype, q, k, v, o, lse, workspace, p, nullptr, stream);
+}
+
+int fa_forward_strided(int impl, int dtype, const void* q, const void* k, const void* v, void* o,
+                       float* lse, void* workspace, const fa_params_t* p, const fa_strides_t* st,
+                       cudaStream_t stream) {
+  if (st == nullptr) return cudaErrorInvalidValue;
+  return forward_impl(impl, dtype, q, k, v, o, lse, workspace, p, st, stream);
 }
 
 }  // extern "C"

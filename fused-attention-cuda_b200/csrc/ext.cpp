@@ -66,8 +66,11 @@ int checked_int(int64_t v, const char* what) {
 }
 
 // Input contract (reference ext.cpp:82-126): every violation is a RuntimeError, never a fault.
+// With `strided`, q/k/v may be any [B, H, N, D] views whose head dim is contiguous and whose other
+// strides are positive multiples of 16 bytes (no counterpart in the reference, which requires
+// contiguous inputs).
 fa_params_t make_params(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
-                        bool is_causal, double scale) {
+                        bool is_causal, double scale, bool strided = false) {
   TORCH_CHECK(q.is_cuda() && k.is_cuda() && v.is_cuda(),
               "fused_attn: q, k, v must be CUDA tensors");
   TORCH_CHECK(q.device() == k.device() && q.device() == v.device(),
@@ -75,8 +78,20 @@ fa_params_t make_params(const at::Tensor& q, const at::Tensor& k, const at::Tens
   TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4,
               "fused_attn: q, k, v must be [B, H, N, D]; got ", q.dim(), "-D, ", k.dim(), "-D, ",
               v.dim(), "-D");
-  TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous(),
-              "fused_attn: q, k, v must be contiguous [B, H, N, D] (call .contiguous())");
+  if (!strided) {
+    TORCH_CHECK(q.is_contiguous() && k.is_contiguous() && v.is_contiguous(),
+                "fused_attn: q, k, v must be contiguous [B, H, N, D] (call .contiguous())");
+  } else {
+    for (const at::Tensor* t : {&q, &k, &v}) {
+      TORCH_CHECK(t->dim() == 4 && t->stride(3) == 1,
+                  "fused_attn: strided views need a contiguous head dim (stride(3) == 1)");
+      for (int d = 0; d < 3; ++d) {
+        TORCH_CHECK(t->stride(d) > 0 && (t->stride(d) * t->element_size()) % 16 == 0,
+                    "fused_attn: strided views need positive strides that are multiples of 16 "
+                    "bytes; got stride(", d, ") = ", t->stride(d));
+      }
+    }
+  }
   for (const at::Tensor* t : {&q, &k, &v}) {
     TORCH_CHECK(reinterpret_cast<std::uintptr_t>(t->data_ptr()) % 16 == 0,
                 "fused_attn: q/k/v must be 16-byte aligned (use a fresh contiguous tensor)");
@@ -113,9 +128,9 @@ fa_params_t make_params(const at::Tensor& q, const at::Tensor& k, const at::Tens
 
 std::tuple<at::Tensor, at::Tensor> run_stage(const at::Tensor& q, const at::Tensor& k,
                                              const at::Tensor& v, bool is_causal, double scale,
-                                             int64_t stage) {
+                                             int64_t stage, bool strided = false) {
   check_stage(stage);
-  const fa_params_t p = make_params(q, k, v, is_causal, scale);
+  const fa_params_t p = make_params(q, k, v, is_causal, scale, strided);
   const c10::cuda::CUDAGuard guard(q.device());
   const int impl = static_cast<int>(stage);
   const int dtype = to_fa_dtype(q.scalar_type());
@@ -124,6 +139,8 @@ std::tuple<at::Tensor, at::Tensor> run_stage(const at::Tensor& q, const at::Tens
               fa_impl_name(impl), ") is not implemented for ", fa_dtype_name(dtype), " D=", p.D,
               " on sm_", sm);
 
+  // O takes q's layout (empty_like keeps the strides of a dense view, e.g. the [B, H, N, D]
+  // transpose of a [B, N, H, D] buffer), so a head merge after the op is a free view too.
   at::Tensor o = at::empty_like(q);
   const bool has_lse = stage >= kFirstLseStage;
   at::Tensor lse = has_lse ? at::empty({p.B, p.H, p.N}, q.options().dtype(at::kFloat))
@@ -136,8 +153,21 @@ std::tuple<at::Tensor, at::Tensor> run_stage(const at::Tensor& q, const at::Tens
     ws_ptr = workspace.data_ptr();
   }
   const cudaStream_t stream = at::cuda::getCurrentCUDAStream(q.device().index()).stream();
-  const int err = fa_forward(impl, dtype, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
-                             has_lse ? lse.data_ptr<float>() : nullptr, ws_ptr, &p, stream);
+  int err;
+  if (strided) {
+    TORCH_CHECK(o.stride(3) == 1, "fused_attn: output layout has a non-contiguous head dim");
+    fa_strides_t st;
+    const at::Tensor* ts[4] = {&q, &k, &v, &o};
+    long long* dst[4] = {st.q, st.k, st.v, st.o};
+    for (int t = 0; t < 4; ++t) {
+      for (int d = 0; d < 3; ++d) dst[t][d] = static_cast<long long>(ts[t]->stride(d));
+    }
+    err = fa_forward_strided(impl, dtype, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                             has_lse ? lse.data_ptr<float>() : nullptr, ws_ptr, &p, &st, stream);
+  } else {
+    err = fa_forward(impl, dtype, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
+                     has_lse ? lse.data_ptr<float>() : nullptr, ws_ptr, &p, stream);
+  }
   TORCH_CHECK(err == 0, "fused_attn: stage ", stage, " (", fa_impl_name(impl),
               ") failed: ", cudaGetErrorString(static_cast<cudaError_t>(err)));
   return std::make_tuple(std::move(o), std::move(lse));
@@ -154,6 +184,24 @@ std::tuple<at::Tensor, at::Tensor> forward_cuda(const at::Tensor& q, const at::T
   for (int64_t stage = kMaxStage; stage >= kFirstLseStage; --stage) {
     if (fa_impl_supports(static_cast<int>(stage), dtype, p.D, sm)) {
       return run_stage(q, k, v, is_causal, scale, stage);
+    }
+  }
+  TORCH_CHECK(false, "fused_attn: no stage is implemented for ", fa_dtype_name(dtype), " D=", p.D,
+              " on sm_", sm);
+  return {};
+}
+
+// forward over strided [B, H, N, D] views (no counterpart in the reference): same stage choice.
+std::tuple<at::Tensor, at::Tensor> forward_strided_cuda(const at::Tensor& q, const at::Tensor& k,
+                                                        const at::Tensor& v, bool is_causal,
+                                                        double scale) {
+  const fa_params_t p = make_params(q, k, v, is_causal, scale, true);
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int dtype = to_fa_dtype(q.scalar_type());
+  const int sm = current_sm();
+  for (int64_t stage = kMaxStage; stage >= kFirstLseStage; --stage) {
+    if (fa_impl_supports(static_cast<int>(stage), dtype, p.D, sm)) {
+      return run_stage(q, k, v, is_causal, scale, stage, true);
     }
   }
   TORCH_CHECK(false, "fused_attn: no stage is implemented for ", fa_dtype_name(dtype), " D=", p.D,
@@ -188,6 +236,9 @@ std::string impl_name_op(int64_t stage) {
 TORCH_LIBRARY(fused_attn, m) {
   m.def("forward(Tensor q, Tensor k, Tensor v, bool is_causal, float scale) -> (Tensor, Tensor)");
   m.def(
+      "forward_strided(Tensor q, Tensor k, Tensor v, bool is_causal, float scale)"
+      " -> (Tensor, Tensor)");
+  m.def(
       "forward_stage(Tensor q, Tensor k, Tensor v, bool is_causal, float scale, int stage)"
       " -> (Tensor, Tensor)");
   m.def("set_debug_overrides(int block_m, int block_n) -> ()", &set_debug_overrides_op);
@@ -197,6 +248,7 @@ TORCH_LIBRARY(fused_attn, m) {
 
 TORCH_LIBRARY_IMPL(fused_attn, CUDA, m) {
   m.impl("forward", &forward_cuda);
+  m.impl("forward_strided", &forward_strided_cuda);
   m.impl("forward_stage", &forward_stage_cuda);
 }
 

@@ -251,8 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (i >= args.n_items) break;
         const Item item = decode_item<CAUSAL>(i, args);
         const int q0 = item.q_tile * kBlockM;
-        const int b_idx = item.bh / args.H;
-        const int bh_kv = b_idx * args.Hkv + (item.bh - b_idx * args.H) / (args.H / args.Hkv);
+        const Heads hd = split_heads(item.bh, args);
         const int kv_end = CAUSAL ? min(args.N, q0 + kBlockM) : args.N;
         const int n_rounds = (kv_end + BR - 1) / BR;
         if (is_k) {
@@ -265,8 +264,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(bar(L::kBarQFull), L::kQBytes);
 #pragma unroll
           for (int c = 0; c < L::kDChunks; ++c) {
-            tma_load_3d(sbase + L::kQOff + c * L::kQChunkBytes, &tm_q, c * 64, q0, item.bh,
-                        bar(L::kBarQFull));
+            tma_load_view(sbase + L::kQOff + c * L::kQChunkBytes, &tm_q, c * 64, q0, hd.h, hd.b,
+                          args.q_pos, bar(L::kBarQFull));
           }
           ++items_done;
         }
@@ -284,8 +283,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(bar(bar_full + s), L::kKVBytes);
 #pragma unroll
           for (int c = 0; c < L::kDChunks; ++c) {
-            tma_load_3d(ring + s * L::kKVBytes + c * L::kKVChunkBytes, tm, c * 64, j * BR, bh_kv,
-                        bar(bar_full + s));
+            tma_load_view(ring + s * L::kKVBytes + c * L::kKVChunkBytes, tm, c * 64, j * BR, hd.hk,
+                          hd.b, is_k ? args.k_pos : args.v_pos, bar(bar_full + s));
           }
         }
       }
@@ -574,8 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
       const float f0 = a0 * inv_l, f1 = a1 * inv_l;
       const bool in_range = row < args.N;
-      T* orow = reinterpret_cast<T*>(args.o) +
-                (static_cast<size_t>(item.bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)) * D;
+      T* orow = out_row<T>(args, item.bh, row);
       // Each warpgroup normalises and stores half of the head dimension.
 #pragma unroll
       for (int c = g * (D / 2); c < (g + 1) * (D / 2); c += 32) {

@@ -214,8 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (i >= args.n_items) break;
         const Item item = decode_item<CAUSAL>(i, args);
         const int q0 = item.q_tile * kBlockM;
-        const int b_idx = item.bh / args.H;
-        const int bh_kv = b_idx * args.Hkv + (item.bh - b_idx * args.H) / (args.H / args.Hkv);
+        const Heads hd = split_heads(item.bh, args);
         const int kv_end = CAUSAL ? min(args.N, q0 + kBlockM) : args.N;
         const int n_tiles = (kv_end + BN - 1) / BN;
         if (is_k) {
@@ -228,8 +227,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(bar(L::kBarQFull), L::kQBytes);
 #pragma unroll
           for (int c = 0; c < L::kDChunks; ++c) {
-            tma_load_3d(sbase + L::kQOff + c * L::kQChunkBytes, &tm_q, c * L::kSwElems, q0,
-                        item.bh, bar(L::kBarQFull));
+            tma_load_view(sbase + L::kQOff + c * L::kQChunkBytes, &tm_q, c * L::kSwElems, q0,
+                          hd.h, hd.b, args.q_pos, bar(L::kBarQFull));
           }
           ++items_done;
         }
@@ -247,8 +246,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_arrive_expect_tx(bar(bar_full + s), L::kKVBytes);
 #pragma unroll
           for (int c = 0; c < L::kDChunks; ++c) {
-            tma_load_3d(ring + s * L::kKVBytes + c * L::kKVChunkBytes, tm, c * L::kSwElems,
-                        j * BN, bh_kv, bar(bar_full + s));
+            tma_load_view(ring + s * L::kKVBytes + c * L::kKVChunkBytes, tm, c * L::kSwElems,
+                          j * BN, hd.hk, hd.b, is_k ? args.k_pos : args.v_pos, bar(bar_full + s));
           }
         }
       }
@@ -499,8 +498,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
       const float f0 = a0 * inv_l, f1 = a1 * inv_l;
       const bool in_range = row < args.N;
-      T* orow = reinterpret_cast<T*>(args.o) +
-                (static_cast<size_t>(item.bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)) * D;
+      T* orow = out_row<T>(args, item.bh, row);
       // Each group normalises and stores half of the head dimension.
 #pragma unroll
       for (int c = g * (D / 2); c < (g + 1) * (D / 2); c += 32) {
@@ -557,16 +555,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // fp32 inputs would enter the tf32 tensor core with their low 13 mantissa bits dropped
 // (truncation: a bias toward zero that shifts every score the same way).  The fp32 path first
-// rounds q, k and v to tf32 (round to nearest, ties away) into the caller's workspace, laid out
-// [q | k | v], so the products carry unbiased rounding errors.  HBM-bound: 16 bytes in and out
-// per thread and step, grid-stride.
+// rounds q, k and v to tf32 (round to nearest, ties away) into the caller's workspace as
+// contiguous [B, H, N, D] copies laid out [q | k | v], gathering from any (b, h, n) strides, so
+// the products carry unbiased rounding errors.  HBM-bound: 16 bytes in and out per thread and
+// step, grid-stride.
+struct View4 {
+  const float* p;
+  long long sb, sh, sn;  // element strides; d contiguous
+  int heads;
+  size_t units;          // 16-byte units of the contiguous copy
+};
+
+__device__ __forceinline__ uint4 load_view_unit(const View4& v, size_t u, int N, int d4) {
+  const size_t row = u / d4;  // (b * heads + h) * N + n
+  const int c = static_cast<int>(u - row * d4);
+  const size_t bh = row / N;
+  const int n = static_cast<int>(row - bh * N);
+  const size_t b = bh / v.heads;
+  const int h = static_cast<int>(bh - b * v.heads);
+  const float* src = v.p + b * v.sb + h * v.sh + n * v.sn + 4 * c;
+  return *reinterpret_cast<const uint4*>(src);
+}
+
 __global__ void __launch_bounds__(256)
-    fa_round_tf32_kernel(const uint4* __restrict__ q, size_t nq, const uint4* __restrict__ k,
-                         size_t nk, const uint4* __restrict__ v, size_t nv, uint4* __restrict__ out) {
-  const size_t n = nq + nk + nv;
+    fa_round_tf32_kernel(View4 q, View4 k, View4 v, int N, int d4, uint4* __restrict__ out) {
+  const size_t n = q.units + k.units + v.units;
   const size_t stride = static_cast<size_t>(gridDim.x) * blockDim.x;
   for (size_t i = static_cast<size_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < n; i += stride) {
-    const uint4 x = i < nq ? q[i] : (i < nq + nk ? k[i - nq] : v[i - nq - nk]);
+    const uint4 x = i < q.units ? load_view_unit(q, i, N, d4)
+                    : i < q.units + k.units ? load_view_unit(k, i - q.units, N, d4)
+                                            : load_view_unit(v, i - q.units - k.units, N, d4);
     out[i] = make_uint4(f32_to_tf32(__uint_as_float(x.x)), f32_to_tf32(__uint_as_float(x.y)),
                         f32_to_tf32(__uint_as_float(x.z)), f32_to_tf32(__uint_as_float(x.w)));
   }
@@ -594,23 +612,41 @@ EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// [heads, N, D] view of a contiguous [B, H, N, D] tensor; box = 128 bytes of D x `rows` rows.
-// Rows past N (inside one head) are zero-filled by the TMA unit.
+// [b][h][n][d] view of q/k/v with element strides st = {b, h, n} (d contiguous) as a 4-D tensor
+// map.  Dimension 0 is d (box = 128 bytes of it); dimensions 1-3 are n, h, b sorted by stride
+// (the encoder's layout model has each stride include the previous one); `pos` returns, packed
+// two bits each, the map dimension (0-2 among dims 1-3) holding n, h and b.  Rows past N are
+// zero-filled by the TMA unit.
 cudaError_t make_tmap(CUtensorMap* m, const void* base, CUtensorMapDataType dt, int elem_bytes,
-                      int D, int N, long long heads, int rows,
-                      CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
+                      int D, int N, int heads, int B, int rows, const long long st[3],
+                      CUtensorMapSwizzle swizzle, int* pos) {
   const EncodeTiledFn enc = get_encode_fn();
   if (enc == nullptr) return cudaErrorNotSupported;
-  const cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(N),
-                              static_cast<cuuint64_t>(heads)};
-  const cuuint64_t strides[2] = {static_cast<cuuint64_t>(D) * elem_bytes,
-                                 static_cast<cuuint64_t>(N) * D * elem_bytes};
-  const cuuint32_t box[3] = {static_cast<cuuint32_t>(128 / elem_bytes),
-                             static_cast<cuuint32_t>(rows), 1u};
-  const cuuint32_t estride[3] = {1u, 1u, 1u};
-  const CUresult r = enc(m, dt, 3, const_cast<void*>(base), dims, strides, box, estride,
+  const long long stride[3] = {st[2], st[1], st[0]};  // n, h, b
+  const long long size[3] = {N, heads, B};
+  int order[3] = {0, 1, 2};
+  for (int i = 1; i < 3; ++i) {  // stable insertion sort by stride
+    for (int j = i; j > 0 && stride[order[j]] < stride[order[j - 1]]; --j) {
+      const int t = order[j];
+      order[j] = order[j - 1];
+      order[j - 1] = t;
+    }
+  }
+  cuuint64_t dims[4] = {static_cast<cuuint64_t>(D), 0, 0, 0};
+  cuuint64_t strides[3];
+  cuuint32_t box[4] = {static_cast<cuuint32_t>(128 / elem_bytes), 1u, 1u, 1u};
+  int p = 0;
+  for (int i = 0; i < 3; ++i) {
+    dims[i + 1] = static_cast<cuuint64_t>(size[order[i]]);
+    strides[i] = static_cast<cuuint64_t>(stride[order[i]]) * elem_bytes;
+    if (order[i] == 0) box[i + 1] = static_cast<cuuint32_t>(rows);
+    p |= i << (2 * order[i]);
+  }
+  const cuuint32_t estride[4] = {1u, 1u, 1u, 1u};
+  const CUresult r = enc(m, dt, 4, const_cast<void*>(base), dims, strides, box, estride,
                          CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
                          CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  *pos = p;
   return r == CUDA_SUCCESS ? cudaSuccess : cudaErrorInvalidValue;
 }
 
@@ -649,16 +685,26 @@ cudaError_t prepare(const LaunchArgs& a, int D, int BN, Prepared* pr) {
                                  : std::is_same<T, float>::value ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32
                                                                  : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const long long hq = static_cast<long long>(a.B) * a.H;
-  const long long hkv = static_cast<long long>(a.B) * a.Hkv;
-  if ((e = make_tmap(&pr->mq, a.q, dt, kEB, D, a.N, hq, kBlockM)) != cudaSuccess) return e;
-  if ((e = make_tmap(&pr->mk, a.k, dt, kEB, D, a.N, hkv, BN)) != cudaSuccess) return e;
-  // tf32 V is an MN-major operand: 32-byte swizzle atoms (see sdesc_sw128_atom32).
-  const CUtensorMapSwizzle v_swizzle =
-      kEB == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
-  if ((e = make_tmap(&pr->mv, a.v, dt, kEB, D, a.N, hkv, BN, v_swizzle)) != cudaSuccess) return e;
-
   KArgs& ka = pr->ka;
+  const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  if ((e = make_tmap(&pr->mq, a.q, dt, kEB, D, a.N, a.H, a.B, kBlockM, a.sq, sw, &ka.q_pos)) !=
+      cudaSuccess) {
+    return e;
+  }
+  if ((e = make_tmap(&pr->mk, a.k, dt, kEB, D, a.N, a.Hkv, a.B, BN, a.sk, sw, &ka.k_pos)) !=
+      cudaSuccess) {
+    return e;
+  }
+  // tf32 V is an MN-major operand: 32-byte swizzle atoms (see sdesc_sw128_atom32).
+  const CUtensorMapSwizzle v_swizzle = kEB == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : sw;
+  if ((e = make_tmap(&pr->mv, a.v, dt, kEB, D, a.N, a.Hkv, a.B, BN, a.sv, v_swizzle, &ka.v_pos)) !=
+      cudaSuccess) {
+    return e;
+  }
   ka.o = a.o;
+  ka.o_sb = a.so[0];
+  ka.o_sh = a.so[1];
+  ka.o_sn = a.so[2];
   ka.lse = a.lse;
   ka.H = a.H;
   ka.Hkv = a.Hkv;
@@ -824,24 +870,35 @@ cudaError_t launch_forward(const LaunchArgs& a, cudaStream_t stream) {
 namespace {
 cudaError_t launch_f32(const LaunchArgs& a, cudaStream_t s) {
   if (a.workspace == nullptr) return cudaErrorInvalidValue;
-  const size_t nq = static_cast<size_t>(a.B) * a.H * a.N * a.D / 4;  // 16-byte units
-  const size_t nkv = static_cast<size_t>(a.B) * a.Hkv * a.N * a.D / 4;
+  const int d4 = a.D / 4;  // 16-byte units per row
+  const size_t nq = static_cast<size_t>(a.B) * a.H * a.N * d4;
+  const size_t nkv = static_cast<size_t>(a.B) * a.Hkv * a.N * d4;
   uint4* ws = static_cast<uint4*>(a.workspace);
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  const View4 vq{static_cast<const float*>(a.q), a.sq[0], a.sq[1], a.sq[2], a.H, nq};
+  const View4 vk{static_cast<const float*>(a.k), a.sk[0], a.sk[1], a.sk[2], a.Hkv, nkv};
+  const View4 vv{static_cast<const float*>(a.v), a.sv[0], a.sv[1], a.sv[2], a.Hkv, nkv};
   const size_t n = nq + 2 * nkv;
   const size_t want = (n + 255) / 256;
   const size_t cap = static_cast<size_t>(sm_count_of(dev)) * 8;
   const unsigned int grid = static_cast<unsigned int>(want < cap ? want : cap);
-  fa_round_tf32_kernel<<<grid, 256, 0, s>>>(static_cast<const uint4*>(a.q), nq,
-                                             static_cast<const uint4*>(a.k), nkv,
-                                             static_cast<const uint4*>(a.v), nkv, ws);
+  fa_round_tf32_kernel<<<grid, 256, 0, s>>>(vq, vk, vv, a.N, d4, ws);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  // The kernel then reads the contiguous copies; o keeps the caller's strides.
   LaunchArgs r = a;
   r.q = ws;
   r.k = ws + nq;
   r.v = ws + nq + nkv;
+  const long long nd = static_cast<long long>(a.N) * a.D;
+  const long long cq[3] = {static_cast<long long>(a.H) * nd, nd, a.D};
+  const long long ckv[3] = {static_cast<long long>(a.Hkv) * nd, nd, a.D};
+  for (int i = 0; i < 3; ++i) {
+    r.sq[i] = cq[i];
+    r.sk[i] = ckv[i];
+    r.sv[i] = ckv[i];
+  }
   return launch_t<float>(r, s);
 }
 }  // namespace

@@ -42,7 +42,9 @@ constexpr float kRescaleThreshold = 8.0f;
 
 struct KArgs {
   void* o;
-  float* lse;
+  long long o_sb, o_sh, o_sn;  // element strides of o's (b, h, n) dimensions (d is contiguous)
+  float* lse;                  // [B, H, N] contiguous
+  int q_pos, k_pos, v_pos;     // tensor-map dimension (2 bits each) holding n, h, b
   int H, Hkv, N;
   int n_q_tiles;
   int n_bh;        // B * H
@@ -63,6 +65,34 @@ struct KArgs {
 struct Item {
   int bh, q_tile;
 };
+
+// (batch, query head, kv head) of flattened head index bh = b * H + h.
+struct Heads {
+  int b, h, hk;
+};
+__device__ __forceinline__ Heads split_heads(int bh, const KArgs& a) {
+  const int b = bh / a.H;
+  const int h = bh - b * a.H;
+  return Heads{b, h, h / (a.H / a.Hkv)};
+}
+
+// TMA load of one box of a [b][h][n][d] view whose map orders n, h, b by stride (`pos`).
+__device__ __forceinline__ void tma_load_view(uint32_t dst, const void* tmap, int x, int n, int h,
+                                              int b, int pos, uint32_t bar) {
+  const int pn = pos & 3, ph = (pos >> 2) & 3;
+  const int c0 = pn == 0 ? n : (ph == 0 ? h : b);
+  const int c1 = pn == 1 ? n : (ph == 1 ? h : b);
+  const int c2 = pn == 2 ? n : (ph == 2 ? h : b);
+  tma_load_4d(dst, tmap, x, c0, c1, c2, bar);
+}
+
+// First element of output row `row` of head bh.
+template <typename T>
+__device__ __forceinline__ T* out_row(const KArgs& a, int bh, int row) {
+  const Heads hd = split_heads(bh, a);
+  return reinterpret_cast<T*>(a.o) + hd.b * a.o_sb + hd.h * a.o_sh +
+         static_cast<long long>(row) * a.o_sn;
+}
 
 __device__ __forceinline__ int item_index(int round, int G, int c) {
   return round * G + ((round & 1) ? (G - 1 - c) : c);

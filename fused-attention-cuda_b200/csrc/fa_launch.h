@@ -22,6 +22,8 @@ struct LaunchArgs {
   unsigned long long timeout_ns;
   int skip_kv_tile;  // fault injection, -1 = off
   void* workspace;   // fp32 only: tf32-rounded q|k|v, workspace_bytes_f32() bytes
+  // Element strides of the (b, h, n) dimensions of q, k, v, o; d is contiguous.
+  long long sq[3], sk[3], sv[3], so[3];
 };
 
 // Which key-tile widths this build instantiates for (dtype, D).

@@ -88,6 +88,16 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int 
       : "memory");
 }
 
+// 4-D tiled load {x = innermost, y, z, w}: the [b][h][n][d] view of q/k/v with arbitrary strides.
+__device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int x, int y, int z,
+                                            int w, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3, %4, %5}], [%6];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
+      : "memory");
+}
+
 // Same, with an L2 cache-policy hint (createpolicy result).
 __device__ __forceinline__ void tma_load_3d_hint(uint32_t dst, const void* tmap, int x, int y,
                                                  int z, uint32_t bar, uint64_t policy) {

@@ -5,6 +5,7 @@ functions, same validation messages.  The ops (registered by ``fused_attn._C``):
 
     torch.ops.fused_attn.forward(q, k, v, is_causal, scale) -> (O, LSE)
     torch.ops.fused_attn.forward_stage(q, k, v, is_causal, scale, stage) -> (O, LSE)
+    torch.ops.fused_attn.forward_strided(q, k, v, is_causal, scale) -> (O, LSE)   [B200 addition]
     torch.ops.fused_attn.set_debug_overrides(block_m, block_n) -> ()
     torch.ops.fused_attn.impl_supports(stage, dtype_name, D) -> bool
     torch.ops.fused_attn.impl_name(stage) -> str
@@ -29,6 +30,7 @@ __all__ = [
     "debug_set_skip_kv_tile",
     "forward",
     "forward_stage",
+    "forward_strided",
     "impl_name",
     "impl_supports",
     "is_available",
@@ -79,6 +81,23 @@ def forward(q: Tensor, k: Tensor, v: Tensor, is_causal: bool = False, scale: flo
     ``(o, lse)`` with ``return_lse=True``; the raw op always returns both."""
     _require_ext()
     o, lse = torch.ops.fused_attn.forward(q, k, v, bool(is_causal), _resolve_scale(q, scale))
+    return (o, lse) if return_lse else o
+
+
+def forward_strided(q: Tensor, k: Tensor, v: Tensor, is_causal: bool = False,
+                    scale: float | None = None, return_lse: bool = False):
+    """``forward`` on [B, H, N, D] views with any strides whose head dim is contiguous (no
+    counterpart in the reference, which needs contiguous inputs).  A GPT-style projection
+    ``x[B, T, 3*H*D]`` splits into heads with ``view`` + ``transpose`` only, and the output has
+    q's layout, so merging the heads back is a view as well::
+
+        q, k, v = qkv.view(B, T, 3, H, D).permute(2, 0, 3, 1, 4)   # no copy
+        o = fused_attn.forward_strided(q, k, v, is_causal=True)     # [B, H, T, D] view
+        y = o.transpose(1, 2).reshape(B, T, H * D)                   # no copy
+    """
+    _require_ext()
+    o, lse = torch.ops.fused_attn.forward_strided(q, k, v, bool(is_causal),
+                                                  _resolve_scale(q, scale))
     return (o, lse) if return_lse else o
 
 

@@ -17,6 +17,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libfa_sm100.so"
 # against the library's exported symbols).
 EXPORTS = (
     "fa_forward",
+    "fa_forward_strided",
     "fa_workspace_bytes",
     "fa_impl_supports",
     "fa_set_debug_overrides",
@@ -52,6 +53,13 @@ class FaParams(ctypes.Structure):
     ]
 
 
+class FaStrides(ctypes.Structure):
+    """``fa_strides_t``: element strides of the (b, h, n) dims of q, k, v, o (d contiguous)."""
+
+    _fields_ = [("q", ctypes.c_longlong * 3), ("k", ctypes.c_longlong * 3),
+                ("v", ctypes.c_longlong * 3), ("o", ctypes.c_longlong * 3)]
+
+
 _lib: ctypes.CDLL | None = None
 
 
@@ -71,6 +79,9 @@ def lib() -> ctypes.CDLL:
         vp, i, u = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint
         L.fa_forward.argtypes = [i, i, vp, vp, vp, vp, vp, vp, ctypes.POINTER(FaParams), vp]
         L.fa_forward.restype = i
+        L.fa_forward_strided.argtypes = [i, i, vp, vp, vp, vp, vp, vp, ctypes.POINTER(FaParams),
+                                         ctypes.POINTER(FaStrides), vp]
+        L.fa_forward_strided.restype = i
         L.fa_workspace_bytes.argtypes = [i, i, ctypes.POINTER(FaParams)]
         L.fa_workspace_bytes.restype = ctypes.c_size_t
         L.fa_impl_supports.argtypes = [i, i, i, i]
@@ -104,6 +115,23 @@ def forward(impl: int, dtype: int, q: int, k: int, v: int, o: int, lse: int, p: 
     """Raw ``fa_forward`` on device pointers (ints); returns the cudaError_t value."""
     return int(lib().fa_forward(impl, dtype, q, k, v, o, lse, workspace or None,
                                 ctypes.byref(p), stream or None))
+
+
+def strides(q, k, v, o) -> FaStrides:
+    """FaStrides of four [B, H, N, D] tensors (anything with ``.stride()``)."""
+    st = FaStrides()
+    for name, t in (("q", q), ("k", k), ("v", v), ("o", o)):
+        sb, sh, sn, _ = t.stride()
+        getattr(st, name)[:] = [int(sb), int(sh), int(sn)]
+    return st
+
+
+def forward_strided(impl: int, dtype: int, q: int, k: int, v: int, o: int, lse: int,
+                    p: FaParams, st: FaStrides | None, stream: int = 0, workspace: int = 0) -> int:
+    """Raw ``fa_forward_strided``; ``st=None`` passes NULL (an invalid-value error)."""
+    return int(lib().fa_forward_strided(impl, dtype, q, k, v, o, lse, workspace or None,
+                                        ctypes.byref(p), ctypes.byref(st) if st is not None else None,
+                                        stream or None))
 
 
 def impl_supports(impl: int, dtype: int, D: int, sm: int) -> bool:

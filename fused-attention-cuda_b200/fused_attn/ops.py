@@ -40,6 +40,13 @@ def _fake_forward(q: Tensor, k: Tensor, v: Tensor, is_causal: bool, scale: float
     return torch.empty_like(q), q.new_empty((b, h, n), dtype=torch.float32)
 
 
+def _fake_forward_strided(q: Tensor, k: Tensor, v: Tensor, is_causal: bool, scale: float):
+    # O takes q's layout (empty_like keeps a dense view's strides), LSE is contiguous.
+    _check_inputs(q, k, v)
+    b, h, n, _ = q.shape
+    return torch.empty_like(q), q.new_empty((b, h, n), dtype=torch.float32)
+
+
 def _fake_forward_stage(q: Tensor, k: Tensor, v: Tensor, is_causal: bool, scale: float, stage: int):
     _check_inputs(q, k, v)
     torch._check(1 <= stage <= 5, lambda: f"stage must be in 1..5, got {stage}")
@@ -59,6 +66,7 @@ def register_fakes() -> None:
         return
     torch.library.register_fake("fused_attn::forward", _fake_forward)
     torch.library.register_fake("fused_attn::forward_stage", _fake_forward_stage)
+    torch.library.register_fake("fused_attn::forward_strided", _fake_forward_strided)
     _registered = True
 
 
@@ -88,6 +96,8 @@ def opcheck_all(q: Tensor, k: Tensor, v: Tensor, is_causal: bool = False,
         scale = 1.0 / (q.shape[-1] ** 0.5)
     results: dict[str, dict[str, str]] = {}
     results["forward"] = _opcheck(torch.ops.fused_attn.forward, (q, k, v, is_causal, float(scale)))
+    results["forward_strided"] = _opcheck(torch.ops.fused_attn.forward_strided,
+                                          (q, k, v, is_causal, float(scale)))
     for stage in stages:
         results[f"forward_stage[{stage}]"] = _opcheck(
             torch.ops.fused_attn.forward_stage, (q, k, v, is_causal, float(scale), int(stage))

@@ -62,6 +62,24 @@ typedef struct fa_params {
 int fa_forward(int impl, int dtype, const void* q, const void* k, const void* v, void* o,
                float* lse, void* workspace, const fa_params_t* p, cudaStream_t stream);
 
+/* No counterpart in the reference (whose API takes contiguous tensors only): element strides of
+ * the (b, h, n) dimensions of q, k, v and o; the head dim d is contiguous.  Views such as the
+ * [B, H, N, D] transpose of a [B, N, H, D] (GPT-style [B, T, H*D]) buffer are read and written in
+ * place, without .contiguous() copies.  Each stride must be positive and a multiple of 16 bytes;
+ * o must not overlap itself or the inputs. */
+typedef struct fa_strides {
+  long long q[3];
+  long long k[3];
+  long long v[3];
+  long long o[3];
+} fa_strides_t;
+
+/* fa_forward over strided views (see fa_strides_t); lse stays contiguous [B, H, N].  Same
+ * return codes as fa_forward; bad strides are cudaErrorInvalidValue. */
+int fa_forward_strided(int impl, int dtype, const void* q, const void* k, const void* v, void* o,
+                       float* lse, void* workspace, const fa_params_t* p, const fa_strides_t* st,
+                       cudaStream_t stream);
+
 /* fa::workspace_bytes (attention.cuh:51; src/dispatch.cu:163-168).  0 for fp16/bf16.  For fp32
  * (FA_IMPL_FUSED, tf32 tensor cores) 4*D*N*(B*H + 2*B*Hkv) bytes: q, k and v rounded to tf32
  * (round to nearest) before the kernel reads them, instead of the tensor core's truncation. */

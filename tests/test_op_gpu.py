@@ -11,6 +11,7 @@ import pytest
 import torch
 
 import fused_attn
+from fused_attn import ops
 from fused_attn.ops import opcheck_all
 
 pytestmark = pytest.mark.gpu
@@ -27,13 +28,38 @@ def require(dtype=torch.float16, d=64):
 
 @pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
 @pytest.mark.parametrize("dtype", DTYPES, ids=["fp16", "bf16"])
-def test_opcheck_both_ops(dtype, causal, make_qkv):
+def test_opcheck_all_ops(dtype, causal, make_qkv):
     require(dtype)
     q, k, v = make_qkv(1, 2, 64, 64, dtype=dtype, device="cuda")
     results = opcheck_all(q, k, v, is_causal=causal, stages=[5])
-    assert set(results) == {"forward", "forward_stage[5]"}
+    assert set(results) == {"forward", "forward_strided", "forward_stage[5]"}
     for name, res in results.items():
         assert all(status in ("SUCCESS", "SKIPPED") for status in res.values()), (name, res)
+
+
+def test_opcheck_strided_op_on_views():
+    """opcheck of forward_strided on non-contiguous head-split views (fake kernel = real layout)."""
+    require(torch.float16, 64)
+    x = torch.randn(1, 64, 3, 2, 64, device="cuda", dtype=torch.float16)
+    q, k, v = x.permute(2, 0, 3, 1, 4)
+    res = ops._opcheck(torch.ops.fused_attn.forward_strided, (q, k, v, True, 0.125))
+    assert all(status in ("SUCCESS", "SKIPPED") for status in res.values()), res
+
+
+def test_compile_fullgraph_gpt_head_split_without_copies():
+    """torch.compile(fullgraph=True) of split-heads -> forward_strided -> merge-heads."""
+    require(torch.float16, 64)
+    b, t, h, d = 2, 128, 4, 64
+
+    def block(qkv):
+        q, k, v = qkv.view(b, t, 3, h, d).permute(2, 0, 3, 1, 4)
+        o = fused_attn.forward_strided(q, k, v, is_causal=True)
+        return o.transpose(1, 2).reshape(b, t, h * d)
+
+    x = torch.randn(b, t, 3 * h * d, device="cuda", dtype=torch.float16)
+    eager = block(x)
+    compiled = torch.compile(block, fullgraph=True)(x)
+    assert torch.equal(eager, compiled)
 
 
 @pytest.mark.parametrize("dtype", DTYPES, ids=["fp16", "bf16"])
