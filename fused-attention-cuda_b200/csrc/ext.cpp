@@ -24,6 +24,7 @@
 #include <limits>
 #include <string>
 #include <tuple>
+#include <vector>
 
 #include "fa_sm100.h"
 
@@ -215,6 +216,47 @@ std::tuple<at::Tensor, at::Tensor> forward_stage_cuda(const at::Tensor& q, const
   return run_stage(q, k, v, is_causal, scale, stage);
 }
 
+// LSE-weighted merge of partials over disjoint key sets (no counterpart in the reference).
+std::tuple<at::Tensor, at::Tensor> combine_cuda(at::TensorList o_parts, at::TensorList lse_parts) {
+  TORCH_CHECK(!o_parts.empty() && o_parts.size() == lse_parts.size(),
+              "fused_attn: combine needs as many LSE tensors as O partials (at least one)");
+  TORCH_CHECK(o_parts.size() <= FA_COMBINE_MAX_SPLITS, "fused_attn: combine takes at most ",
+              FA_COMBINE_MAX_SPLITS, " partials, got ", o_parts.size());
+  const at::Tensor& o0 = o_parts[0];
+  TORCH_CHECK(o0.is_cuda() && o0.dim() == 4, "fused_attn: partials must be CUDA [B, H, N, D]");
+  const int64_t B = o0.size(0), H = o0.size(1), N = o0.size(2), D = o0.size(3);
+  TORCH_CHECK(D == 64 || D == 128, "fused_attn: D must be 64 or 128, got ", D);
+  std::vector<const void*> op;
+  std::vector<const float*> lp;
+  for (size_t i = 0; i < o_parts.size(); ++i) {
+    const at::Tensor& o = o_parts[i];
+    const at::Tensor& l = lse_parts[i];
+    TORCH_CHECK(o.device() == o0.device() && l.device() == o0.device(),
+                "fused_attn: combine inputs must live on one device");
+    TORCH_CHECK(o.sizes() == o0.sizes() && o.scalar_type() == o0.scalar_type() &&
+                    o.is_contiguous(),
+                "fused_attn: O partials must be contiguous with one shape and dtype");
+    TORCH_CHECK(l.scalar_type() == at::kFloat && l.is_contiguous() && l.dim() == 3 &&
+                    l.size(0) == B && l.size(1) == H && l.size(2) == N,
+                "fused_attn: LSE partials must be contiguous fp32 [B, H, N]");
+    TORCH_CHECK(reinterpret_cast<std::uintptr_t>(o.data_ptr()) % 16 == 0,
+                "fused_attn: O partials must be 16-byte aligned");
+    op.push_back(o.data_ptr());
+    lp.push_back(l.data_ptr<float>());
+  }
+  const c10::cuda::CUDAGuard guard(o0.device());
+  at::Tensor out = at::empty_like(o0, at::MemoryFormat::Contiguous);
+  at::Tensor lse = at::empty({B, H, N}, o0.options().dtype(at::kFloat));
+  const cudaStream_t stream = at::cuda::getCurrentCUDAStream(o0.device().index()).stream();
+  const int err = fa_combine(to_fa_dtype(o0.scalar_type()), static_cast<int>(op.size()), op.data(),
+                             lp.data(), out.data_ptr(), lse.data_ptr<float>(),
+                             checked_int(B, "B"), checked_int(H, "H"), checked_int(N, "N"),
+                             checked_int(D, "D"), stream);
+  TORCH_CHECK(err == 0, "fused_attn: combine failed: ",
+              cudaGetErrorString(static_cast<cudaError_t>(err)));
+  return std::make_tuple(std::move(out), std::move(lse));
+}
+
 void set_debug_overrides_op(int64_t block_m, int64_t block_n) {
   fa_set_debug_overrides(checked_int(block_m, "block_m"), checked_int(block_n, "block_n"));
 }
@@ -241,6 +283,7 @@ TORCH_LIBRARY(fused_attn, m) {
   m.def(
       "forward_stage(Tensor q, Tensor k, Tensor v, bool is_causal, float scale, int stage)"
       " -> (Tensor, Tensor)");
+  m.def("combine(Tensor[] o_parts, Tensor[] lse_parts) -> (Tensor, Tensor)");
   m.def("set_debug_overrides(int block_m, int block_n) -> ()", &set_debug_overrides_op);
   m.def("impl_supports(int stage, str dtype, int D) -> bool", &impl_supports_op);
   m.def("impl_name(int stage) -> str", &impl_name_op);
@@ -249,6 +292,7 @@ TORCH_LIBRARY(fused_attn, m) {
 TORCH_LIBRARY_IMPL(fused_attn, CUDA, m) {
   m.impl("forward", &forward_cuda);
   m.impl("forward_strided", &forward_strided_cuda);
+  m.impl("combine", &combine_cuda);
   m.impl("forward_stage", &forward_stage_cuda);
 }
 

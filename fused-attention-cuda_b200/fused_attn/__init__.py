@@ -6,6 +6,7 @@ functions, same validation messages.  The ops (registered by ``fused_attn._C``):
     torch.ops.fused_attn.forward(q, k, v, is_causal, scale) -> (O, LSE)
     torch.ops.fused_attn.forward_stage(q, k, v, is_causal, scale, stage) -> (O, LSE)
     torch.ops.fused_attn.forward_strided(q, k, v, is_causal, scale) -> (O, LSE)   [B200 addition]
+    torch.ops.fused_attn.combine(o_parts, lse_parts) -> (O, LSE)                 [B200 addition]
     torch.ops.fused_attn.set_debug_overrides(block_m, block_n) -> ()
     torch.ops.fused_attn.impl_supports(stage, dtype_name, D) -> bool
     torch.ops.fused_attn.impl_name(stage) -> str
@@ -27,6 +28,7 @@ from . import abi, ops, workloads
 __all__ = [
     "__version__",
     "abi",
+    "combine",
     "debug_set_skip_kv_tile",
     "forward",
     "forward_stage",
@@ -99,6 +101,21 @@ def forward_strided(q: Tensor, k: Tensor, v: Tensor, is_causal: bool = False,
     o, lse = torch.ops.fused_attn.forward_strided(q, k, v, bool(is_causal),
                                                   _resolve_scale(q, scale))
     return (o, lse) if return_lse else o
+
+
+def combine(o_parts, lse_parts) -> tuple[Tensor, Tensor]:
+    """Merge attention partials of the same queries over disjoint key sets (split-KV, ring /
+    context-parallel attention): ``lse = ln sum exp(lse_i)``, ``o = sum exp(lse_i - lse) o_i``.
+    ``o_parts``: contiguous [B, H, N, D] tensors, ``lse_parts``: fp32 [B, H, N] as returned by
+    ``forward(..., return_lse=True)``.  Causal self-attention over a sequence split into chunks
+    c = 0..S-1 is, chunk by chunk::
+
+        parts = [fused_attn.forward(q[c], k[j], v[j], is_causal=(j == c), return_lse=True)
+                 for j in range(c + 1)]
+        o_c, lse_c = fused_attn.combine(*zip(*parts))
+    """
+    _require_ext()
+    return torch.ops.fused_attn.combine(list(o_parts), list(lse_parts))
 
 
 def forward_stage(q: Tensor, k: Tensor, v: Tensor, stage: int, is_causal: bool = False,

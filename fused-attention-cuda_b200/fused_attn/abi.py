@@ -18,6 +18,7 @@ LIB_PATH = Path(__file__).resolve().parent / "libfa_sm100.so"
 EXPORTS = (
     "fa_forward",
     "fa_forward_strided",
+    "fa_combine",
     "fa_workspace_bytes",
     "fa_impl_supports",
     "fa_set_debug_overrides",
@@ -82,6 +83,9 @@ def lib() -> ctypes.CDLL:
         L.fa_forward_strided.argtypes = [i, i, vp, vp, vp, vp, vp, vp, ctypes.POINTER(FaParams),
                                          ctypes.POINTER(FaStrides), vp]
         L.fa_forward_strided.restype = i
+        L.fa_combine.argtypes = [i, i, ctypes.POINTER(vp), ctypes.POINTER(vp), vp, vp, i, i, i, i,
+                                 vp]
+        L.fa_combine.restype = i
         L.fa_workspace_bytes.argtypes = [i, i, ctypes.POINTER(FaParams)]
         L.fa_workspace_bytes.restype = ctypes.c_size_t
         L.fa_impl_supports.argtypes = [i, i, i, i]
@@ -132,6 +136,18 @@ def forward_strided(impl: int, dtype: int, q: int, k: int, v: int, o: int, lse: 
     return int(lib().fa_forward_strided(impl, dtype, q, k, v, o, lse, workspace or None,
                                         ctypes.byref(p), ctypes.byref(st) if st is not None else None,
                                         stream or None))
+
+
+COMBINE_MAX_SPLITS = 64
+
+
+def combine(dtype: int, o_parts: list[int], lse_parts: list[int], o: int, lse: int, B: int,
+            H: int, N: int, D: int, stream: int = 0) -> int:
+    """Raw ``fa_combine`` on device pointers; returns the cudaError_t value."""
+    n = len(o_parts)
+    op = (ctypes.c_void_p * max(n, 1))(*o_parts)
+    lp = (ctypes.c_void_p * max(n, 1))(*lse_parts)
+    return int(lib().fa_combine(dtype, n, op, lp, o, lse, B, H, N, D, stream or None))
 
 
 def impl_supports(impl: int, dtype: int, D: int, sm: int) -> bool:

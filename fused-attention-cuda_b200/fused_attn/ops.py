@@ -47,6 +47,15 @@ def _fake_forward_strided(q: Tensor, k: Tensor, v: Tensor, is_causal: bool, scal
     return torch.empty_like(q), q.new_empty((b, h, n), dtype=torch.float32)
 
 
+def _fake_combine(o_parts, lse_parts):
+    torch._check(len(o_parts) >= 1 and len(o_parts) == len(lse_parts),
+                 lambda: "combine needs as many LSE tensors as O partials")
+    o0 = o_parts[0]
+    b, h, n, _ = o0.shape
+    return torch.empty_like(o0, memory_format=torch.contiguous_format), \
+        o0.new_empty((b, h, n), dtype=torch.float32)
+
+
 def _fake_forward_stage(q: Tensor, k: Tensor, v: Tensor, is_causal: bool, scale: float, stage: int):
     _check_inputs(q, k, v)
     torch._check(1 <= stage <= 5, lambda: f"stage must be in 1..5, got {stage}")
@@ -67,6 +76,7 @@ def register_fakes() -> None:
     torch.library.register_fake("fused_attn::forward", _fake_forward)
     torch.library.register_fake("fused_attn::forward_stage", _fake_forward_stage)
     torch.library.register_fake("fused_attn::forward_strided", _fake_forward_strided)
+    torch.library.register_fake("fused_attn::combine", _fake_combine)
     _registered = True
 
 

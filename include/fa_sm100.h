@@ -80,6 +80,20 @@ int fa_forward_strided(int impl, int dtype, const void* q, const void* k, const 
                        float* lse, void* workspace, const fa_params_t* p, const fa_strides_t* st,
                        cudaStream_t stream);
 
+/* No counterpart in the reference, whose roadmap lists split-KV decoding with an LSE-weighted
+ * combine (the reason the forward returns LSE, attention.cuh:39-40).  Merges n_splits partial
+ * results of the same queries over disjoint key sets -- e.g. the steps of ring / context-parallel
+ * attention, or KV chunks computed separately:
+ *   lse = ln sum_i exp(lse_i),  o = sum_i exp(lse_i - lse) * o_i.
+ * o_parts / lse_parts are HOST arrays of n_splits device pointers to contiguous [B, H, N, D]
+ * partials of `dtype` (16-byte aligned) and [B, H, N] fp32 natural-log LSEs; a partial row with
+ * lse = +inf or -inf saw no key and gets weight 0; a row with no keys anywhere gets o = 0,
+ * lse = +inf (the forward's convention, softmax_math.cuh:64-68).  Writes contiguous o and lse,
+ * which must not alias the partials.  D is 64 or 128; 1 <= n_splits <= FA_COMBINE_MAX_SPLITS. */
+#define FA_COMBINE_MAX_SPLITS 64
+int fa_combine(int dtype, int n_splits, const void* const* o_parts, const float* const* lse_parts,
+               void* o, float* lse, int B, int H, int N, int D, cudaStream_t stream);
+
 /* fa::workspace_bytes (attention.cuh:51; src/dispatch.cu:163-168).  0 for fp16/bf16.  For fp32
  * (FA_IMPL_FUSED, tf32 tensor cores) 4*D*N*(B*H + 2*B*Hkv) bytes: q, k and v rounded to tf32
  * (round to nearest) before the kernel reads them, instead of the tensor core's truncation. */

@@ -243,6 +243,28 @@ def numpy_attention(q, k, v, causal: bool = False, scale: float | None = None, k
     return o, lse[..., 0]
 
 
+def combine(o_parts, lse_parts):
+    """LSE-weighted merge of attention partials over disjoint key sets, fp64:
+    lse = ln sum_i exp(lse_i), o = sum_i exp(lse_i - lse) o_i.  A partial row with lse = +inf
+    (the forward's "saw no key" value, cpu_reference.cpp / softmax_math.cuh:64-68) or -inf has
+    weight 0; a row with no keys anywhere gives o = 0, lse = +inf.  The reference has no combine
+    of its own (its roadmap lists one); this restates the math it implies, and the CPU tests pin
+    it to ``numpy_attention`` on the unsplit keys."""
+    lse = np.stack([_as_f64(x) for x in lse_parts])  # [S, B, H, N]
+    o = np.stack([_as_f64(x) for x in o_parts])      # [S, B, H, N, D]
+    empty = ~np.isfinite(lse)
+    m = np.where(empty, -np.inf, lse).max(axis=0)
+    has = np.isfinite(m)
+    m_safe = np.where(has, m, 0.0)
+    w = np.where(empty, 0.0, np.exp(np.where(empty, 0.0, lse) - m_safe))
+    l = w.sum(axis=0)
+    ok = l > 0
+    out = (w[..., None] * o).sum(axis=0) / np.where(ok, l, 1.0)[..., None]
+    out = np.where(ok[..., None], out, 0.0)
+    lse_out = np.where(ok, m_safe + np.log(np.where(ok, l, 1.0)), np.inf)
+    return out, lse_out
+
+
 def max_abs(a, b) -> float:
     """NaN-aware max |a - b| (cpu_reference.cpp:167-175): NaN anywhere counts as +inf."""
     a64, b64 = _as_f64(a), _as_f64(b)
