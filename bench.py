@@ -510,6 +510,22 @@ def secondary_measurements(cfg, q, k, v, flush, stream, steps):
         out[name] = {"workload": c.label(), "ours_ms": statistics.median(t),
                      "ours_tflops": f2 / statistics.median(t) / 1e9,
                      "sdpa_ms": statistics.median(ts), "sdpa_tflops": f2 / statistics.median(ts) / 1e9}
+    # fp32 inputs (stage 3: tf32 tensor cores after the tf32-rounding pre-pass into the
+    # workspace): the C1 configuration and the C3 shape in fp32.
+    for name, (b_, h_, n_, d_, causal_, seed_) in (("C1c_fp32", (1, 2, 128, 64, True, 0)),
+                                                   ("C3_shape_fp32", (2, 8, 2048, 128, True, 2))):
+        q3, k3, v3 = make_qkv(b_, h_, n_, d_, dtype=torch.float32, seed=seed_, device=q.device)
+        f3 = attention_flops(b_, h_, n_, d_, causal_)
+        s3 = 1.0 / math.sqrt(d_)
+        t = time_kernel(lambda: torch.ops.fused_attn.forward(q3, k3, v3, causal_, s3), steps, 10,
+                        flush, stream)
+        ts = time_kernel(lambda: F.scaled_dot_product_attention(q3, k3, v3, is_causal=causal_),
+                         steps, 10, flush, stream)
+        out[name] = {"workload": f"B{b_}H{h_}N{n_}D{d_} fp32 {'causal' if causal_ else 'full'}",
+                     "path": "stage 3: tf32 rounding pre-pass + tcgen05 kind::tf32",
+                     "ours_ms": statistics.median(t), "ours_tflops": f3 / statistics.median(t) / 1e9,
+                     "sdpa_fp32_ms": statistics.median(ts),
+                     "sdpa_fp32_tflops": f3 / statistics.median(ts) / 1e9}
     return out
 
 
