@@ -35,7 +35,7 @@ ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = [*ARCH_FLAGS, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
               "-Xcompiler", "-Wall", f"-I{INCLUDE}", f"-I{CSRC}"]
 
-KERNEL_SOURCES = ["fa_fwd_sm100.cu", "dispatch.cu", "fa_combine.cu"]
+KERNEL_SOURCES = ["fa_fwd_sm100.cu", "dispatch.cu", "fa_combine.cu", "fa_noalloc.cu"]
 KERNEL_HEADERS = ["sm100_ptx.cuh", "fa_launch.h", "fa_kernel_common.cuh", "fa_fwd_lookahead.cuh"]
 
 LIB_NAME = "libfa_sm100.so"

@@ -19,6 +19,8 @@ EXPORTS = (
     "fa_forward",
     "fa_forward_strided",
     "fa_combine",
+    "fa_forward_noalloc",
+    "fa_noalloc_scratch_bytes",
     "fa_workspace_bytes",
     "fa_impl_supports",
     "fa_set_debug_overrides",
@@ -86,6 +88,10 @@ def lib() -> ctypes.CDLL:
         L.fa_combine.argtypes = [i, i, ctypes.POINTER(vp), ctypes.POINTER(vp), vp, vp, i, i, i, i,
                                  vp]
         L.fa_combine.restype = i
+        L.fa_forward_noalloc.argtypes = [i, i, vp, vp, vp, vp, vp, ctypes.POINTER(FaParams), vp]
+        L.fa_forward_noalloc.restype = i
+        L.fa_noalloc_scratch_bytes.argtypes = []
+        L.fa_noalloc_scratch_bytes.restype = ctypes.c_size_t
         L.fa_workspace_bytes.argtypes = [i, i, ctypes.POINTER(FaParams)]
         L.fa_workspace_bytes.restype = ctypes.c_size_t
         L.fa_impl_supports.argtypes = [i, i, i, i]
@@ -136,6 +142,17 @@ def forward_strided(impl: int, dtype: int, q: int, k: int, v: int, o: int, lse: 
     return int(lib().fa_forward_strided(impl, dtype, q, k, v, o, lse, workspace or None,
                                         ctypes.byref(p), ctypes.byref(st) if st is not None else None,
                                         stream or None))
+
+
+def forward_noalloc(impl: int, dtype: int, q: int, k: int, v: int, o: int, lse: int,
+                    p: FaParams, stream: int = 0) -> int:
+    """Raw ``fa_forward_noalloc`` (scratch from the library's fixed device array)."""
+    return int(lib().fa_forward_noalloc(impl, dtype, q, k, v, o, lse, ctypes.byref(p),
+                                        stream or None))
+
+
+def noalloc_scratch_bytes() -> int:
+    return int(lib().fa_noalloc_scratch_bytes())
 
 
 COMBINE_MAX_SPLITS = 64

@@ -94,6 +94,18 @@ int fa_forward_strided(int impl, int dtype, const void* q, const void* k, const 
 int fa_combine(int dtype, int n_splits, const void* const* o_parts, const float* const* lse_parts,
                void* o, float* lse, int B, int H, int N, int D, cudaStream_t stream);
 
+/* No counterpart in the reference: fa_forward with no workspace argument and no allocation of
+ * any kind.  Paths that need scratch (fp32 on FA_IMPL_FUSED: fa_workspace_bytes > 0) use a fixed
+ * device array of FA_NOALLOC_SCRATCH_BYTES compiled into the library; larger problems return
+ * cudaErrorInvalidValue.  That array is shared by all calls on a device, so calls whose
+ * executions overlap (other streams or host threads) race on it.  Its address is looked up on the
+ * first call on each device, which should therefore happen before any stream capture. */
+#define FA_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)
+int fa_forward_noalloc(int impl, int dtype, const void* q, const void* k, const void* v, void* o,
+                       float* lse, const fa_params_t* p, cudaStream_t stream);
+/* Size of that scratch array in bytes (FA_NOALLOC_SCRATCH_BYTES). */
+size_t fa_noalloc_scratch_bytes(void);
+
 /* fa::workspace_bytes (attention.cuh:51; src/dispatch.cu:163-168).  0 for fp16/bf16.  For fp32
  * (FA_IMPL_FUSED, tf32 tensor cores) 4*D*N*(B*H + 2*B*Hkv) bytes: q, k and v rounded to tf32
  * (round to nearest) before the kernel reads them, instead of the tensor core's truncation. */
