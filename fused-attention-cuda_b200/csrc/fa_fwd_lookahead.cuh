@@ -135,6 +135,15 @@ __device__ __forceinline__ void mbar_arrive_after(uint32_t bar, float dep) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar), "f"(dep) : "memory");
 }
 
+// Every kLaEmuEvery-th pair of exponentials is computed on the FMA pipes (ex2_poly3) instead of
+// the MUFU unit, which both warpgroups saturate during their exponential phase (15.6 exp2/clk/SM
+// measured).  One pair in four measured best on B200 (C3 557 vs 524 TFLOP/s, N=8192 1037 vs 980;
+// one in three or two is slower).  Build-time switch FA_LA_EX2_EMU_EVERY (0 = all on MUFU).
+#ifndef FA_LA_EX2_EMU_EVERY
+#define FA_LA_EX2_EMU_EVERY 4
+#endif
+constexpr int kLaEmuEvery = FA_LA_EX2_EMU_EVERY;
+
 // p = 2^(s*c - m*c) for the 64 columns of one S row, packed two per 32-bit word into pk[32]
 // (and P_lo = p - round(p) into lo[32] when kLo); returns the sum of the fp32 weights.
 template <typename T, bool kLo>
@@ -147,7 +156,8 @@ __device__ __forceinline__ float exp_pack64(const float (&s)[64], float sl2, flo
   for (int c = 0; c < 32; ++c) {
     const uint64_t x = f2_fma(f2_pack(s[2 * c], s[2 * c + 1]), c2, nb2);
     float p0, p1;
-    if (kEmuEvery > 0 && (c % (kEmuEvery > 0 ? kEmuEvery : 1)) == (kEmuEvery > 0 ? kEmuEvery : 1) - 1) {
+    constexpr int kE = kLaEmuEvery > 0 ? kLaEmuEvery : 1;
+    if (kLaEmuEvery > 0 && (c % kE) == kE - 1) {
       p0 = ex2_poly3(f2_lo(x));
       p1 = ex2_poly3(f2_hi(x));
     } else {
