@@ -529,6 +529,97 @@ def secondary_measurements(cfg, q, k, v, flush, stream, steps):
     return out
 
 
+def _cmd_version(cmd: list[str], pick) -> str:
+    try:
+        out = subprocess.run(cmd, capture_output=True, text=True, timeout=20).stdout
+        return pick(out)
+    except (OSError, subprocess.SubprocessError, IndexError, ValueError):
+        return "unknown"
+
+
+def run_sweep(args) -> int:
+    """--sweep OUT.csv: the reference's canonical sweep (CONTRACT.md §5: N in 128..4096, D in
+    {64, 128}, (B, H) in {(1, 8), (8, 32)}, causal 0/1; fp16) plus C3 in bf16, for our kernel and
+    every PyTorch SDPA backend that accepts the shape, written as rows of the reference's frozen
+    CSV schema (fused_attn/benchcsv.py) and rendered to OUT.md.  Our rows carry max_abs against
+    fp32 SDPA on the same inputs."""
+    import torch
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    from fused_attn import benchcsv
+    from fused_attn.workloads import make_qkv
+
+    torch.cuda.set_device(0)
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(256 << 18, dtype=torch.float32, device=dev)
+    env = {
+        "commit": args.commit,
+        "gpu": torch.cuda.get_device_name(0),
+        "driver": _cmd_version(["nvidia-smi", "--query-gpu=driver_version", "--format=csv,noheader",
+                                "--id=0"], lambda o: o.strip().splitlines()[0]),
+        "nvcc": _cmd_version(["nvcc", "--version"],
+                             lambda o: o.split("release")[1].split(",")[0].strip()),
+        "torch": torch.__version__,
+        "ncu": _cmd_version(["ncu", "--version"], lambda o: o.strip().splitlines()[-1].split()[-1]),
+        "clock_mhz": "unlocked",
+    }
+    backends = {"sdpa_flash": SDPBackend.FLASH_ATTENTION,
+                "sdpa_efficient": SDPBackend.EFFICIENT_ATTENTION,
+                "sdpa_cudnn": SDPBackend.CUDNN_ATTENTION}
+    shapes = [(b, h, n, d, c, torch.float16) for (b, h) in ((1, 8), (8, 32))
+              for n in (128, 256, 512, 1024, 2048, 4096) for d in (64, 128) for c in (False, True)]
+    shapes.append((2, 8, 2048, 128, True, torch.bfloat16))
+    rows = []
+    clocks = ClockSampler(0)
+    clocks.start()
+    t_start = time.time()
+    for (b, h, n, d, causal, dt) in shapes:
+        dname = {torch.float16: "fp16", torch.bfloat16: "bf16"}[dt]
+        q, k, v = make_qkv(b, h, n, d, dtype=dt, device=dev, seed=2)
+        scale = 1.0 / math.sqrt(d)
+        with sdpa_kernel([SDPBackend.EFFICIENT_ATTENTION, SDPBackend.MATH]):
+            ref = F.scaled_dot_product_attention(q.float(), k.float(), v.float(), is_causal=causal)
+        o = torch.ops.fused_attn.forward(q, k, v, causal, scale)[0]
+        err = float((o.float() - ref).abs().max())
+        t = time_kernel(lambda: torch.ops.fused_attn.forward(q, k, v, causal, scale),
+                        args.sweep_iters, 10, flush, stream)
+        rows.append(benchcsv.make_row(env, "tuned", dname, b, h, n, d, causal, t,
+                                      [f"max_abs={err:.3e}", "vs=sdpa_fp32"]))
+        for name, be in backends.items():
+            try:
+                with sdpa_kernel([be]):
+                    F.scaled_dot_product_attention(q, k, v, is_causal=causal)
+                    torch.cuda.synchronize()
+                    t = time_kernel(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=causal),
+                                    args.sweep_iters, 10, flush, stream)
+            except RuntimeError:
+                continue  # the backend refuses this shape/dtype: no row
+            rows.append(benchcsv.make_row(env, name, dname, b, h, n, d, causal, t, []))
+        del q, k, v, ref, o
+    clocks.window(t_start, time.time())
+    ck = clocks.stop()
+    if ck and ck.get("sm_mhz"):
+        for r in rows:
+            r["notes"] += f";clock_median={ck['sm_mhz']:.0f}"
+    benchcsv.write_rows(args.sweep, rows)
+    md = Path(args.sweep).with_suffix(".md")
+    md.write_text(benchcsv.to_markdown(rows))
+    hdr, back = benchcsv.read_rows(args.sweep)
+    problems = benchcsv.validate(hdr, back, roof_tflops=_roof_tflops())
+    print(json.dumps({"sweep": str(args.sweep), "rows": len(rows), "problems": problems[:10]}))
+    return 0 if not problems else 1
+
+
+def _roof_tflops() -> float:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["bf16_tflops"])
+    except (OSError, ValueError, KeyError):
+        return 1590.0
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -539,7 +630,13 @@ def main(argv=None) -> int:
     ap.add_argument("--cpu-budget", type=float, default=12.0,
                     help="seconds of CPU oracle work for the cpu_baseline sample")
     ap.add_argument("--quick", action="store_true", help="skip secondary and CPU measurements")
+    ap.add_argument("--sweep", default=None,
+                    help="write the reference-schema sweep CSV (and .md) to this path instead")
+    ap.add_argument("--sweep-iters", type=int, default=100)
+    ap.add_argument("--commit", default="unknown", help="commit SHA recorded in sweep rows")
     args = ap.parse_args(argv)
+    if args.sweep:
+        return run_sweep(args)
     args.warmup = max(args.warmup, 3)  # the timing rules require at least 3 warm-up steps
     if args.impl == "reference":
         return run_reference(args)
