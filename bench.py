@@ -459,7 +459,8 @@ def _pct(xs, p):
 
 def secondary_measurements(cfg, q, k, v, flush, stream, steps):
     """Context numbers (not the headline): PyTorch SDPA on the same inputs and the same
-    protocol, a CUDA-graph batch average of our kernel, and the D64 (C2) configs."""
+    protocol, a CUDA-graph batch average of our kernel, the D64 (C2) configs, the fp32 (stage 3)
+    configs and the GPT-2 block (C5)."""
     import torch
     import torch.nn.functional as F
 
@@ -526,7 +527,39 @@ def secondary_measurements(cfg, q, k, v, flush, stream, steps):
                      "ours_ms": statistics.median(t), "ours_tflops": f3 / statistics.median(t) / 1e9,
                      "sdpa_fp32_ms": statistics.median(ts),
                      "sdpa_fp32_tflops": f3 / statistics.median(ts) / 1e9}
+    out["C5_gpt2_block"] = gpt_block_measurements(q.device)
     return out
+
+
+def gpt_block_measurements(device, warmup: int = 10, iters: int = 50) -> dict:
+    """C5: tokens/s of the GPT-2-small block (token + position embedding, one pre-LN block,
+    d 768, 12 heads of 64, MLP 4x, fp16, batch 16 x T 1024) with the attention through our op
+    (strided views, and the reference's .contiguous() binding path) and through PyTorch SDPA,
+    plus the attention window's share.  Warm, no L2 flush -- the reference harness's protocol
+    for this end-to-end row (bench/gpt_block.py), whose own block takes a random x at batch 8."""
+    import torch
+
+    from fused_attn import gpt_block as gb
+
+    cfg = gb.GPTConfig()
+    ids = gb.token_ids(cfg, device)
+    impls = {}
+    for impl in ("fused_strided", "fused_contiguous", "sdpa_flash", "sdpa_cudnn"):
+        try:
+            model = gb.build_model(cfg, impl, device)
+            m = gb.measure(model, ids, warmup, iters)
+        except RuntimeError as e:  # an SDPA backend that refuses the shape
+            impls[impl] = {"refused": str(e).splitlines()[0][:160]}
+            continue
+        impls[impl] = {k: round(v, 4) for k, v in m.items()}
+        del model
+        torch.cuda.empty_cache()
+    return {"workload": f"GPT-2-small block B{cfg.batch} T{cfg.seq} d{cfg.n_embd} "
+                        f"H{cfg.n_head} D{cfg.head_dim} fp16 causal, token+position embedding",
+            "metric": "tokens/s", "protocol": f"warm, no L2 flush, {warmup} warm-up + {iters} "
+                                              "timed forwards, CUDA-event median",
+            "attention_gflop": cfg.attention_flops() / 1e9, "gemm_gflop": cfg.gemm_flops() / 1e9,
+            "impls": impls}
 
 
 def _cmd_version(cmd: list[str], pick) -> str:
