@@ -121,6 +121,17 @@ class ClockSampler:
     def window(self, t0: float, t1: float) -> None:
         self.t0, self.t1 = t0, t1
 
+    def median_between(self, t0: float, t1: float) -> float | None:
+        """Median SM clock (MHz) of the samples taken between t0 and t1 (wall clock), or None."""
+        sm = []
+        for t, s in list(self.samples):
+            if t0 <= t <= t1:
+                try:
+                    sm.append(float(s[1]))
+                except (ValueError, IndexError):
+                    continue
+        return statistics.median(sm) if sm else None
+
     def stop(self) -> dict | None:
         if self.proc is None:
             return None
@@ -616,26 +627,32 @@ def run_sweep(args) -> int:
             ref = F.scaled_dot_product_attention(q.float(), k.float(), v.float(), is_causal=causal)
         o = torch.ops.fused_attn.forward(q, k, v, causal, scale)[0]
         err = float((o.float() - ref).abs().max())
-        t = time_kernel(lambda: torch.ops.fused_attn.forward(q, k, v, causal, scale),
-                        args.sweep_iters, 10, flush, stream)
+
+        def timed(fn):
+            # A short idle before each series lets the clocks recover from the previous (power-
+            # capped) one, so rows do not inherit their predecessor's clock state; the SM clock
+            # sampled over the series goes into the row's notes.
+            torch.cuda.synchronize()
+            time.sleep(args.sweep_settle)
+            t0 = time.time()
+            t = time_kernel(fn, args.sweep_iters, 10, flush, stream)
+            mhz = clocks.median_between(t0, time.time())
+            return t, ([f"clock_mhz={mhz:.0f}"] if mhz else [])
+
+        t, cn = timed(lambda: torch.ops.fused_attn.forward(q, k, v, causal, scale))
         rows.append(benchcsv.make_row(env, "tuned", dname, b, h, n, d, causal, t,
-                                      [f"max_abs={err:.3e}", "vs=sdpa_fp32"]))
+                                      [f"max_abs={err:.3e}", "vs=sdpa_fp32"] + cn))
         for name, be in backends.items():
             try:
                 with sdpa_kernel([be]):
                     F.scaled_dot_product_attention(q, k, v, is_causal=causal)
-                    torch.cuda.synchronize()
-                    t = time_kernel(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=causal),
-                                    args.sweep_iters, 10, flush, stream)
+                    t, cn = timed(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=causal))
             except RuntimeError:
                 continue  # the backend refuses this shape/dtype: no row
-            rows.append(benchcsv.make_row(env, name, dname, b, h, n, d, causal, t, []))
+            rows.append(benchcsv.make_row(env, name, dname, b, h, n, d, causal, t, cn))
         del q, k, v, ref, o
     clocks.window(t_start, time.time())
-    ck = clocks.stop()
-    if ck and ck.get("sm_mhz"):
-        for r in rows:
-            r["notes"] += f";clock_median={ck['sm_mhz']:.0f}"
+    clocks.stop()
     benchcsv.write_rows(args.sweep, rows)
     md = Path(args.sweep).with_suffix(".md")
     md.write_text(benchcsv.to_markdown(rows))
@@ -666,6 +683,8 @@ def main(argv=None) -> int:
     ap.add_argument("--sweep", default=None,
                     help="write the reference-schema sweep CSV (and .md) to this path instead")
     ap.add_argument("--sweep-iters", type=int, default=100)
+    ap.add_argument("--sweep-settle", type=float, default=0.3,
+                    help="idle seconds before each timed series of the sweep")
     ap.add_argument("--commit", default="unknown", help="commit SHA recorded in sweep rows")
     args = ap.parse_args(argv)
     if args.sweep:
