@@ -174,6 +174,63 @@ __device__ __forceinline__ float exp_pack64(const float (&s)[64], float sl2, flo
   return f2_lo(t) + f2_hi(t);
 }
 
+// bf16 with P carried as P_hi + P_lo: the exponentials of the 64 columns, P_hi stored at `p_addr`
+// and P_lo at `lo_addr`, eight columns at a time.  Only the first causal query tile runs it, so it
+// is a separate (not inlined) function reading the row from a stack copy: inlined, its extra live
+// words raise the register allocation of the whole kernel from 127 to 159-167 and slow every
+// round of bf16 causal launches by 6-9% (measured).  Returns the sum of the fp32 weights.
+template <typename T>
+__device__ __noinline__ float exp_pack64_hilo_store(const float* s, float sl2, float mc,
+                                                    uint32_t p_addr, uint32_t lo_addr) {
+  const uint64_t c2 = f2_pack(sl2, sl2);
+  const uint64_t nb2 = f2_pack(-mc, -mc);
+  uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
+#pragma unroll 1
+  for (int c0 = 0; c0 < 32; c0 += 8) {
+    uint32_t pk[8], lo[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) {
+      const int cc = c0 + c;
+      const uint64_t x = f2_fma(f2_pack(s[2 * cc], s[2 * cc + 1]), c2, nb2);
+      const float p0 = ex2_approx(f2_lo(x));
+      const float p1 = ex2_approx(f2_hi(x));
+      pk[c] = pack2<T>(p0, p1);
+      acc[c & 3] = f2_add(acc[c & 3], f2_pack(p0, p1));
+      lo[c] = pack2<T>(p0 - __uint_as_float(pk[c] << 16), p1 - __uint_as_float(pk[c] & 0xFFFF0000u));
+    }
+    tmem_st8(p_addr + c0, pk);
+    tmem_st8(lo_addr + c0, lo);
+  }
+  const uint64_t t = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
+  return f2_lo(t) + f2_hi(t);
+}
+
+// PV of a bf16 first-causal-tile round (the item's only round, accumulate = 0): for each warpgroup
+// g, once its P is stored, O_g = P_hi,g V_g + P_lo,g V_g.  Not inlined (see the PV issuer).
+template <typename L, uint32_t kIdescPV>
+__device__ __noinline__ bool issue_pv_hilo(uint32_t tmem, uint64_t v_desc, uint32_t bar_pfull,
+                                           uint32_t bar_pvdone, uint32_t parity, const WaitCtx& w) {
+  constexpr int BG = L::BG;
+  for (int g = 0; g < 2; ++g) {
+    if (!wait_bounded(bar_pfull + 8u * g, parity, w, kStPFull)) return false;
+    tc_fence_after();
+    const uint64_t vg = v_desc + static_cast<uint64_t>((g * BG * 128) >> 4);
+    const uint32_t o_tmem = tmem + L::kColO + g * L::kDChunks * 64;
+    const uint32_t pa = tmem + L::kColP + g * (BG / 2);
+    const uint32_t plo = tmem + L::kColS + g * BG;
+#pragma unroll
+    for (int kk = 0; kk < BG / 16; ++kk) {
+      umma_ts(o_tmem, pa + kk * 8, vg + ((kk * 16 * 128) >> 4), kIdescPV, kk > 0 ? 1u : 0u);
+    }
+#pragma unroll
+    for (int kk = 0; kk < BG / 16; ++kk) {
+      umma_ts(o_tmem, plo + kk * 8, vg + ((kk * 16 * 128) >> 4), kIdescPV, 1u);
+    }
+    umma_commit(bar_pvdone + 8u * g);
+  }
+  return true;
+}
+
 template <typename T, int D, int KST, int VST, bool CAUSAL, bool QTMEM>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_lookahead_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -415,33 +472,33 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           const uint64_t v_desc = v_desc0 + static_cast<uint64_t>((s * L::kKVBytes) >> 4);
+          if (kBf16 && cur.comp) {
+            // The first causal query tile (bf16), a single round: P_hi then P_lo (over the
+            // warpgroup's S columns).  Kept apart from the common round below, whose issue code
+            // measured ~8% faster without the P_lo block inside it (C4, bf16).
+            ok = issue_pv_hilo<L, kIdescPV>(tmem, v_desc, bar(L::kBarPFull), bar(L::kBarPVDone),
+                               static_cast<uint32_t>(pv_cnt) & 1u, w);
+          } else {
 #pragma unroll
-          for (int g = 0; g < 2; ++g) {
-            // Each warpgroup's PV goes as soon as its own P is stored.
-            if (!(ok = wait_bounded(bar(L::kBarPFull + g), static_cast<uint32_t>(pv_cnt) & 1u, w,
-                                    kStPFull))) {
-              break;
-            }
-            tc_fence_after();
-            FA_TRACE_EV(cur.local == 0, 1, g, cur.rr);
-            // Warpgroup g's keys are rows 64g .. 64g+63 of the V slot.
-            const uint64_t vg = v_desc + static_cast<uint64_t>((g * BG * 128) >> 4);
-            const uint32_t o_tmem = tmem + L::kColO + g * D;
-            const uint32_t pa = tmem + L::kColP + g * (BG / 2);
-#pragma unroll
-            for (int kk = 0; kk < BG / 16; ++kk) {
-              umma_ts(o_tmem, pa + kk * 8, vg + ((kk * 16 * 128) >> 4), kIdescPV,
-                      (cur.rr > 0 || kk > 0) ? 1u : 0u);
-            }
-            if (cur.comp) {
-              // P_lo, stored over the warpgroup's S columns.
-              const uint32_t plo = tmem + L::kColS + g * BG;
+            for (int g = 0; g < 2; ++g) {
+              // Each warpgroup's PV goes as soon as its own P is stored.
+              if (!(ok = wait_bounded(bar(L::kBarPFull + g), static_cast<uint32_t>(pv_cnt) & 1u, w,
+                                      kStPFull))) {
+                break;
+              }
+              tc_fence_after();
+              FA_TRACE_EV(cur.local == 0, 1, g, cur.rr);
+              // Warpgroup g's keys are rows 64g .. 64g+63 of the V slot.
+              const uint64_t vg = v_desc + static_cast<uint64_t>((g * BG * 128) >> 4);
+              const uint32_t o_tmem = tmem + L::kColO + g * D;
+              const uint32_t pa = tmem + L::kColP + g * (BG / 2);
 #pragma unroll
               for (int kk = 0; kk < BG / 16; ++kk) {
-                umma_ts(o_tmem, plo + kk * 8, vg + ((kk * 16 * 128) >> 4), kIdescPV, 1u);
+                umma_ts(o_tmem, pa + kk * 8, vg + ((kk * 16 * 128) >> 4), kIdescPV,
+                        (cur.rr > 0 || kk > 0) ? 1u : 0u);
               }
+              umma_commit(bar(L::kBarPVDone + g));
             }
-            umma_commit(bar(L::kBarPVDone + g));
           }
           if (!ok) break;
           umma_commit(bar(L::kBarVEmpty + s));
@@ -521,8 +578,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         launder(mc);  // the exponentials may not start before the turn
         uint32_t pk[32], lo[32];
         float rs;
-        if constexpr (kBf16) {
-          rs = comp ? exp_pack64<T, true>(s, sl2, mc, pk, lo) : exp_pack64<T, false>(s, sl2, mc, pk, lo);
+        if (kBf16 && comp) {
+          // P_hi + P_lo (P_lo over the warpgroup's S columns, whose round is in registers).  The
+          // first causal query tile has a single round (t == 0), so nothing reads P_g or S yet:
+          // both go to tensor memory as they are computed.
+          float s_copy[64];
+#pragma unroll
+          for (int c = 0; c < 64; ++c) s_copy[c] = s[c];
+          rs = exp_pack64_hilo_store<T>(s_copy, sl2, mc, tl + p_col, tl + s_col);
         } else {
           rs = exp_pack64<T, false>(s, sl2, mc, pk, lo);
         }
@@ -547,13 +610,9 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        tmem_st16(tl + p_col, &pk[0]);
-        tmem_st16(tl + p_col + 16, &pk[16]);
-        if constexpr (kBf16) {
-          if (comp) {
-            tmem_st16(tl + s_col, &lo[0]);
-            tmem_st16(tl + s_col + 16, &lo[16]);
-          }
+        if (!(kBf16 && comp)) {
+          tmem_st16(tl + p_col, &pk[0]);
+          tmem_st16(tl + p_col + 16, &pk[16]);
         }
         tmem_st_wait();
         tc_fence_before();

@@ -191,42 +191,47 @@ __device__ __forceinline__ float row_max(const float (&s)[BN]) {
 
 // p = 2^(s*c - m*c) for columns [2*C0, 2*C1) of one S row: the exponent argument in packed fp32
 // pairs, the exponential on MUFU (every kEmuEvery-th pair on the FMA pipes), P packed two per
-// 32-bit word and stored to TMEM at `taddr` + C0 (one column per pair).  Returns the sum of the
-// fp32 weights, accumulated in four packed partial sums.  kLo (bf16 only) also stores
+// 32-bit word and stored to TMEM at `taddr` + C0 (one column per pair), sixteen columns at a time
+// as they are computed (eight with P_lo) so that only sixteen packed words are live.  Returns the
+// sum of the fp32 weights, accumulated in four packed partial sums.  kLo (bf16 only) also stores
 // P_lo = p - bf16(p) at `taddr` + BN/2 + C0.
 template <typename T, int BN, int C0, int C1, bool kLo>
 __device__ __forceinline__ float exp_pack_store(const float (&s)[BN], float sl2, float mc,
                                                 uint32_t taddr) {
   static_assert((C1 - C0) % 16 == 0, "column range must be a multiple of 16 pairs");
   constexpr int kN = C1 - C0;
+  constexpr int kChunk = kLo ? 8 : 16;
   const uint64_t c2 = f2_pack(sl2, sl2);
   const uint64_t nb2 = f2_pack(-mc, -mc);
   uint64_t acc[4] = {0ull, 0ull, 0ull, 0ull};
-  uint32_t pk[kN];
-  uint32_t lo[kLo ? kN : 1];
 #pragma unroll
-  for (int c = 0; c < kN; ++c) {
-    const int cc = C0 + c;
-    const uint64_t x = f2_fma(f2_pack(s[2 * cc], s[2 * cc + 1]), c2, nb2);
-    float p0, p1;
-    if (kEmuEvery > 0 && (cc % (kEmuEvery > 0 ? kEmuEvery : 1)) == (kEmuEvery > 0 ? kEmuEvery : 1) - 1) {
-      p0 = ex2_poly3(f2_lo(x));
-      p1 = ex2_poly3(f2_hi(x));
-    } else {
-      p0 = ex2_approx(f2_lo(x));
-      p1 = ex2_approx(f2_hi(x));
+  for (int c0 = 0; c0 < kN; c0 += kChunk) {
+    uint32_t pk[kChunk];
+    uint32_t lo[kLo ? kChunk : 1];
+#pragma unroll
+    for (int c = 0; c < kChunk; ++c) {
+      const int cc = C0 + c0 + c;
+      const uint64_t x = f2_fma(f2_pack(s[2 * cc], s[2 * cc + 1]), c2, nb2);
+      float p0, p1;
+      if (kEmuEvery > 0 && (cc % (kEmuEvery > 0 ? kEmuEvery : 1)) == (kEmuEvery > 0 ? kEmuEvery : 1) - 1) {
+        p0 = ex2_poly3(f2_lo(x));
+        p1 = ex2_poly3(f2_hi(x));
+      } else {
+        p0 = ex2_approx(f2_lo(x));
+        p1 = ex2_approx(f2_hi(x));
+      }
+      pk[c] = pack2<T>(p0, p1);
+      acc[c & 3] = f2_add(acc[c & 3], f2_pack(p0, p1));
+      if constexpr (kLo) {
+        lo[c] = pack2<T>(p0 - __uint_as_float(pk[c] << 16), p1 - __uint_as_float(pk[c] & 0xFFFF0000u));
+      }
     }
-    pk[c] = pack2<T>(p0, p1);
-    acc[c & 3] = f2_add(acc[c & 3], f2_pack(p0, p1));
     if constexpr (kLo) {
-      lo[c] = pack2<T>(p0 - __uint_as_float(pk[c] << 16), p1 - __uint_as_float(pk[c] & 0xFFFF0000u));
+      tmem_st8(taddr + C0 + c0, pk);
+      tmem_st8(taddr + BN / 2 + C0 + c0, lo);
+    } else {
+      tmem_st16(taddr + C0 + c0, pk);
     }
-  }
-#pragma unroll
-  for (int c = 0; c < kN; c += 16) tmem_st16(taddr + C0 + c, &pk[c]);
-  if constexpr (kLo) {
-#pragma unroll
-    for (int c = 0; c < kN; c += 16) tmem_st16(taddr + BN / 2 + C0 + c, &lo[c]);
   }
   const uint64_t t = f2_add(f2_add(acc[0], acc[1]), f2_add(acc[2], acc[3]));
   return f2_lo(t) + f2_hi(t);
