@@ -52,9 +52,13 @@ struct LaLayout {
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kQBytes;
   static constexpr int kVOff = kKOff + KST * kKVBytes;
-  static constexpr int kXchOff = kVOff + VST * kKVBytes;
+  // O staging for the TMA store of the epilogue: kDChunks 128-byte-swizzled 128-row chunks, like
+  // the Q tile.  The merge's (m, l) exchange lives at its start: it is read before O is staged.
+  static constexpr int kOStOff = kVOff + VST * kKVBytes;
+  static constexpr int kOStBytes = kBlockM * D * 2;
+  static constexpr int kXchOff = kOStOff;
   static constexpr int kXchBytes = 2 * 2 * kBlockM * 4 + 16;
-  static constexpr int kBarOff = kXchOff + kXchBytes;
+  static constexpr int kBarOff = kOStOff + kOStBytes;
 
   // Barrier indices.
   static constexpr int kBarQFull = 0;   // TMA: Q tile landed in shared memory
@@ -87,6 +91,7 @@ struct LaLayout {
   static_assert(D == 64 || D == 128, "head dim");
   static_assert(kColsUsed <= 512, "tensor memory overflow");
   static_assert(kSmemAlloc <= 232448, "shared memory overflow");
+  static_assert(kXchBytes <= kOStBytes, "exchange must fit inside the O staging buffer");
 };
 
 // Walks the CTA's items round by round.
@@ -235,7 +240,8 @@ template <typename T, int D, int KST, int VST, bool CAUSAL, bool QTMEM>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_lookahead_kernel(const __grid_constant__ CUtensorMap tm_q,
                             const __grid_constant__ CUtensorMap tm_k,
-                            const __grid_constant__ CUtensorMap tm_v, const KArgs args) {
+                            const __grid_constant__ CUtensorMap tm_v,
+                            const __grid_constant__ CUtensorMap tm_o, const KArgs args) {
   using L = LaLayout<D, KST, VST>;
   constexpr int BR = L::BR;
   constexpr int BG = L::BG;
@@ -524,6 +530,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sl2 = args.scale_log2;
     float* xch = reinterpret_cast<float*>(smem + L::kXchOff);
     volatile int* xch_ctl = reinterpret_cast<volatile int*>(smem + L::kXchOff + 2 * 2 * kBlockM * 4);
+    const bool o_issuer = (g == 0 && warp == kSoftmaxWarp0 && lane == 0);  // O's TMA stores
+    if (o_issuer) tma_prefetch_desc(&tm_o);
     int sc = 0;   // S rounds consumed, over all items
     int pvc = 0;  // PV rounds waited for, over all items
     int ec = 0;   // exponential phases run by this warpgroup, over all items
@@ -619,12 +627,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         FA_TRACE_EV(rnd == 0 && r == 0, 3, g, t);
         mbar_arrive(bar(L::kBarPFull + g));
       }
-      // ---- merge the two partials and write O / LSE --------------------------------------
+      // ---- merge the two partials; O / l staged in shared memory and written by TMA; LSE ----
       if (ok) {  // the item's last PV round
         ok = __all_sync(0xffffffffu, wait_bounded(bar(L::kBarPVDone + g),
                                                   static_cast<uint32_t>(pvc) & 1u, w, kStODone));
         ++pvc;
       }
+      // The previous item's O store must have read the staging buffer (the exchange lives there).
+      if (o_issuer) bulk_wait_read();
       tc_fence_before();
       named_barrier_sync(kMergeBarrier, 2 * kBlockM);
       xch[(g * 2 + 0) * kBlockM + r] = m_ref;
@@ -642,8 +652,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
       const float f0 = a0 * inv_l, f1 = a1 * inv_l;
       const bool in_range = row < args.N;
-      T* orow = out_row<T>(args, item.bh, row);
-      // Each warpgroup normalises and stores half of the head dimension.
+      // Every thread has read the exchange before O overwrites it.
+      named_barrier_sync(kMergeBarrier, 2 * kBlockM);
+      // Each warpgroup normalises half of the head dimension into the staging buffer: row r of
+      // 64-column chunk c at kOStOff + c*16 KB + r*128 B, 16-byte units XOR-swizzled by r % 8 (the
+      // layout of the O tensor map's 128-byte swizzle).
 #pragma unroll
       for (int c = g * (D / 2); c < (g + 1) * (D / 2); c += 32) {
         uint32_t u0[32], u1[32];
@@ -657,22 +670,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         uint32_t pk[16];
 #pragma unroll
         for (int k2 = 0; k2 < 16; ++k2) pk[k2] = pack2<T>(o[2 * k2], o[2 * k2 + 1]);
-        if (in_range) {
-          uint4* dst = reinterpret_cast<uint4*>(orow + c);
+        uint8_t* rowp = smem + L::kOStOff + (c / 64) * L::kQChunkBytes + r * 128;
 #pragma unroll
-          for (int k2 = 0; k2 < 4; ++k2) {
-            dst[k2] = make_uint4(pk[4 * k2], pk[4 * k2 + 1], pk[4 * k2 + 2], pk[4 * k2 + 3]);
-          }
+        for (int k2 = 0; k2 < 4; ++k2) {
+          const int unit = (c % 64) / 8 + k2;
+          *reinterpret_cast<uint4*>(rowp + ((unit ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * k2], pk[4 * k2 + 1], pk[4 * k2 + 2], pk[4 * k2 + 3]);
         }
-      }
-      if (g == 0 && in_range) {
-        args.lse[static_cast<size_t>(item.bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)] =
-            (l > 0.f && m != -INFINITY) ? fmaf(m, args.scale, logf(l)) : INFINITY;
       }
       // O_0 and O_1 have been read: the next item's first PVs may overwrite them.
       tc_fence_before();
       mbar_arrive(bar(L::kBarOFree));
+      if (g == 0 && in_range) {
+        args.lse[static_cast<size_t>(item.bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)] =
+            (l > 0.f && m != -INFINITY) ? fmaf(m, args.scale, logf(l)) : INFINITY;
+      }
+      // The staged tile goes out in one TMA store per 64-column chunk (rows past N are clipped);
+      // it overlaps the next item.
+      fence_proxy_async_smem();
+      named_barrier_sync(kMergeBarrier, 2 * kBlockM);
+      if (o_issuer) {
+        const Heads hd = split_heads(item.bh, args);
+#pragma unroll
+        for (int c = 0; c < L::kDChunks; ++c) {
+          tma_store_view(&tm_o, sbase + L::kOStOff + c * L::kQChunkBytes, c * 64, q0, hd.h, hd.b,
+                         args.o_pos);
+        }
+        bulk_commit();
+      }
     }
+    // The last O store must have completed before the CTA exits.
+    if (o_issuer) bulk_wait_all();
   }
 
   tc_fence_before();

@@ -670,6 +670,7 @@ struct Prepared {
   alignas(64) CUtensorMap mq;
   alignas(64) CUtensorMap mk;
   alignas(64) CUtensorMap mv;
+  alignas(64) CUtensorMap mo;  // O, 128-row boxes (kernels that store O by TMA)
   KArgs ka;
   int grid;
   int dev;
@@ -686,6 +687,7 @@ cudaError_t prepare(const LaunchArgs& a, int D, int BN, Prepared* pr) {
                                                                  : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   const long long hq = static_cast<long long>(a.B) * a.H;
   KArgs& ka = pr->ka;
+  ka.o_pos = 0;
   const CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
   if ((e = make_tmap(&pr->mq, a.q, dt, kEB, D, a.N, a.H, a.B, kBlockM, a.sq, sw, &ka.q_pos)) !=
       cudaSuccess) {
@@ -699,6 +701,10 @@ cudaError_t prepare(const LaunchArgs& a, int D, int BN, Prepared* pr) {
   const CUtensorMapSwizzle v_swizzle = kEB == 4 ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : sw;
   if ((e = make_tmap(&pr->mv, a.v, dt, kEB, D, a.N, a.Hkv, a.B, BN, a.sv, v_swizzle, &ka.v_pos)) !=
       cudaSuccess) {
+    return e;
+  }
+  if (kEB == 2 && (e = make_tmap(&pr->mo, a.o, dt, kEB, D, a.N, a.H, a.B, kBlockM, a.so, sw,
+                                 &ka.o_pos)) != cudaSuccess) {
     return e;
   }
   ka.o = a.o;
@@ -770,7 +776,7 @@ cudaError_t launch_lookahead(const LaunchArgs& a, cudaStream_t stream) {
   cudaError_t e = prepare<T>(a, D, L::BR, &pr);
   if (e != cudaSuccess) return e;
   if ((e = opt_in_smem(kern, L::kSmemAlloc, &configured, pr.dev)) != cudaSuccess) return e;
-  kern<<<pr.grid, kThreads, L::kSmemAlloc, stream>>>(pr.mq, pr.mk, pr.mv, pr.ka);
+  kern<<<pr.grid, kThreads, L::kSmemAlloc, stream>>>(pr.mq, pr.mk, pr.mv, pr.mo, pr.ka);
   return cudaGetLastError();
 }
 

@@ -45,6 +45,7 @@ struct KArgs {
   long long o_sb, o_sh, o_sn;  // element strides of o's (b, h, n) dimensions (d is contiguous)
   float* lse;                  // [B, H, N] contiguous
   int q_pos, k_pos, v_pos;     // tensor-map dimension (2 bits each) holding n, h, b
+  int o_pos;                   // the same for the output map (kernels that store O by TMA)
   int H, Hkv, N;
   int n_q_tiles;
   int n_bh;        // B * H
@@ -84,6 +85,17 @@ __device__ __forceinline__ void tma_load_view(uint32_t dst, const void* tmap, in
   const int c1 = pn == 1 ? n : (ph == 1 ? h : b);
   const int c2 = pn == 2 ? n : (ph == 2 ? h : b);
   tma_load_4d(dst, tmap, x, c0, c1, c2, bar);
+}
+
+// TMA store of one box from shared memory into the [b][h][n][d] view of O (same coordinate
+// order as tma_load_view).
+__device__ __forceinline__ void tma_store_view(const void* tmap, uint32_t src, int x, int n, int h,
+                                               int b, int pos) {
+  const int pn = pos & 3, ph = (pos >> 2) & 3;
+  const int c0 = pn == 0 ? n : (ph == 0 ? h : b);
+  const int c1 = pn == 1 ? n : (ph == 1 ? h : b);
+  const int c2 = pn == 2 ? n : (ph == 2 ? h : b);
+  tma_store_4d(tmap, x, c0, c1, c2, src);
 }
 
 // First element of output row `row` of head bh.

@@ -98,6 +98,33 @@ __device__ __forceinline__ void tma_load_4d(uint32_t dst, const void* tmap, int 
       : "memory");
 }
 
+// 4-D tiled store of one box from shared memory (bulk-group completion).  Rows past the tensor's
+// extent are not written.  The shared source must not change until bulk_wait_read() returns.
+__device__ __forceinline__ void tma_store_4d(const void* tmap, int x, int y, int z, int w,
+                                             uint32_t src) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
+          reinterpret_cast<uint64_t>(tmap)),
+      "r"(x), "r"(y), "r"(z), "r"(w), "r"(src)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() {
+  asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+}
+// The committed bulk stores have finished reading their shared-memory sources.
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+}
+// The committed bulk stores have completed.
+__device__ __forceinline__ void bulk_wait_all() {
+  asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy accesses (a
+// TMA store that reads them).
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
 // Same, with an L2 cache-policy hint (createpolicy result).
 __device__ __forceinline__ void tma_load_3d_hint(uint32_t dst, const void* tmap, int x, int y,
                                                  int z, uint32_t bar, uint64_t policy) {
