@@ -92,9 +92,14 @@ struct Layout {
   static constexpr int kQOff = 0;
   static constexpr int kKOff = kQOff + kQBytes;
   static constexpr int kVOff = kKOff + KST * kKVBytes;
-  static constexpr int kXchOff = kVOff + VST * kKVBytes;  // merge exchange: m, l per row and group
+  // 16-bit: O staging for the epilogue's TMA store (128-byte-swizzled 128-row chunks of 64
+  // columns, like the Q tile), with the merge's (m, l) exchange at its start -- it is read before
+  // O is staged.  fp32 stores O directly and keeps only the exchange.
+  static constexpr int kOStOff = kVOff + VST * kKVBytes;
   static constexpr int kXchBytes = 2 * 2 * kBlockM * 4 + 16;
-  static constexpr int kBarOff = kXchOff + kXchBytes;
+  static constexpr int kOStBytes = EB == 2 ? kBlockM * D * 2 : kXchBytes;
+  static constexpr int kXchOff = kOStOff;  // merge exchange: m, l per row and group
+  static constexpr int kBarOff = kOStOff + kOStBytes;
   static constexpr int kNumBars = 10 + 2 * KST + 2 * VST;
   static constexpr int kMiscOff = kBarOff + 8 * kNumBars;
   static constexpr int kBytes = kMiscOff + 16;
@@ -139,7 +144,8 @@ template <typename T, int D, int BN, int KST, int VST, bool CAUSAL>
 __global__ void __launch_bounds__(kThreads, 1)
     fa_fwd_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                         const __grid_constant__ CUtensorMap tm_k,
-                        const __grid_constant__ CUtensorMap tm_v, const KArgs args) {
+                        const __grid_constant__ CUtensorMap tm_v,
+                        const __grid_constant__ CUtensorMap tm_o, const KArgs args) {
   using L = Layout<static_cast<int>(sizeof(T)), D, BN, KST, VST>;
   constexpr bool kTf32 = std::is_same<T, float>::value;
   constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : (kTf32 ? 2u : 0u);
@@ -400,6 +406,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     const float sl2 = args.scale_log2;
     float* xch = reinterpret_cast<float*>(smem + L::kXchOff);
     volatile int* xch_ctl = reinterpret_cast<volatile int*>(smem + L::kXchOff + 2 * 2 * kBlockM * 4);
+    // The thread that issues O's TMA stores (16-bit; fp32 writes O directly).
+    const bool o_issuer = !kTf32 && g == 0 && warp == kSoftmaxWarp0 && lane == 0;
+    if (o_issuer) tma_prefetch_desc(&tm_o);
     int sc = 0;   // S tiles consumed by this group, over all items
     int pvc = 0;  // item-final PV completions consumed by this group
     for (int rnd = 0;; ++rnd) {
@@ -473,12 +482,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         FA_TRACE_EV(rnd == 0 && r == 0, 3, g, t);
         mbar_arrive(bar(L::kBarPFull + g));
       }
-      // ---- merge the two partials and write O / LSE --------------------------------------
+      // ---- merge the two partials; O / LSE (16-bit: O staged and written by TMA) ----------
       if (ok && n_t > 0) {  // committed once per item, after the group's last PV
         ok = __all_sync(0xffffffffu, wait_bounded(bar(L::kBarPVDone + g),
                                                   static_cast<uint32_t>(pvc) & 1u, w, kStODone));
         ++pvc;
       }
+      // The previous item's O store must have read the staging buffer (the exchange lives there).
+      if (o_issuer) bulk_wait_read();
       tc_fence_before();
       // Both groups reach both named barriers once per item, on the abort path too; whether to
       // merge and go on is decided by one thread and read by all after the second barrier.
@@ -498,8 +509,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
       const float f0 = a0 * inv_l, f1 = a1 * inv_l;
       const bool in_range = row < args.N;
+      if constexpr (!kTf32) {
+        // Every thread has read the exchange before O overwrites it.
+        named_barrier_sync(kMergeBarrier, 2 * kBlockM);
+      }
       T* orow = out_row<T>(args, item.bh, row);
-      // Each group normalises and stores half of the head dimension.
+      // Each group normalises half of the head dimension: fp32 straight to global memory; 16-bit
+      // into the staging buffer (row r of 64-column chunk c at kOStOff + c*16 KB + r*128 B, 16-byte
+      // units XOR-swizzled by r % 8, the layout of the O tensor map's 128-byte swizzle).
 #pragma unroll
       for (int c = g * (D / 2); c < (g + 1) * (D / 2); c += 32) {
         uint32_t u0[32];
@@ -525,23 +542,40 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t pk[16];
 #pragma unroll
           for (int k2 = 0; k2 < 16; ++k2) pk[k2] = pack2<T>(o[2 * k2], o[2 * k2 + 1]);
-          if (in_range) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + c);
+          uint8_t* rowp = smem + L::kOStOff + (c / 64) * L::kQChunkBytes + r * 128;
 #pragma unroll
-            for (int k2 = 0; k2 < 4; ++k2) {
-              dst[k2] = make_uint4(pk[4 * k2], pk[4 * k2 + 1], pk[4 * k2 + 2], pk[4 * k2 + 3]);
-            }
+          for (int k2 = 0; k2 < 4; ++k2) {
+            const int unit = (c % 64) / 8 + k2;
+            *reinterpret_cast<uint4*>(rowp + ((unit ^ (r & 7)) << 4)) =
+                make_uint4(pk[4 * k2], pk[4 * k2 + 1], pk[4 * k2 + 2], pk[4 * k2 + 3]);
           }
         }
-      }
-      if (g == 0 && in_range) {
-        args.lse[static_cast<size_t>(item.bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)] =
-            (l > 0.f && m != -INFINITY) ? fmaf(m, args.scale, logf(l)) : INFINITY;
       }
       // O_0 and O_1 have been read: the next item's first PVs may overwrite them.
       tc_fence_before();
       mbar_arrive(bar(L::kBarOFree));
+      if (g == 0 && in_range) {
+        args.lse[static_cast<size_t>(item.bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)] =
+            (l > 0.f && m != -INFINITY) ? fmaf(m, args.scale, logf(l)) : INFINITY;
+      }
+      if constexpr (!kTf32) {
+        // The staged tile goes out in one TMA store per 64-column chunk (rows past N are
+        // clipped); it overlaps the next item.
+        fence_proxy_async_smem();
+        named_barrier_sync(kMergeBarrier, 2 * kBlockM);
+        if (o_issuer) {
+          const Heads hd = split_heads(item.bh, args);
+#pragma unroll
+          for (int c = 0; c < L::kDChunks; ++c) {
+            tma_store_view(&tm_o, sbase + L::kOStOff + c * L::kQChunkBytes, c * 64, q0, hd.h, hd.b,
+                           args.o_pos);
+          }
+          bulk_commit();
+        }
+      }
     }
+    // The last O store must have completed before the CTA exits.
+    if (o_issuer) bulk_wait_all();
   }
 
   tc_fence_before();
@@ -759,7 +793,7 @@ cudaError_t launch_impl(const LaunchArgs& a, cudaStream_t stream) {
   cudaError_t e = prepare<T>(a, D, BN, &pr);
   if (e != cudaSuccess) return e;
   if ((e = opt_in_smem(kern, L::kSmemAlloc, &configured, pr.dev)) != cudaSuccess) return e;
-  kern<<<pr.grid, kThreads, L::kSmemAlloc, stream>>>(pr.mq, pr.mk, pr.mv, pr.ka);
+  kern<<<pr.grid, kThreads, L::kSmemAlloc, stream>>>(pr.mq, pr.mk, pr.mv, pr.mo, pr.ka);
   return cudaGetLastError();
 }
 
