@@ -138,7 +138,7 @@ int fa_impl_supports(int impl, int dtype, int D, int sm) {
     default:
       return 0;
   }
-  return fa_sm100::block_n_supported(dtype, D, fa_sm100::default_block_n(dtype, D, 0)) ? 1 : 0;
+  return fa_sm100::block_n_supported(dtype, D, fa_sm100::default_block_n(dtype, D, 0, 0)) ? 1 : 0;
 }
 
 // 0 for fp16/bf16.  fp32 (Impl::Fused) stages tf32-rounded copies of q, k, v in the workspace.
@@ -229,7 +229,7 @@ int forward_impl(int impl, int dtype, const void* q, const void* k, const void* 
     if (verbose()) std::fprintf(stderr, "fa_forward: block_m=%d is not built (0 or 128)\n", bm);
     return cudaErrorInvalidValue;
   }
-  if (bn == 0) bn = fa_sm100::default_block_n(dtype, p->D, p->N);
+  if (bn == 0) bn = fa_sm100::default_block_n(dtype, p->D, p->N, p->causal);
   if (!fa_sm100::block_n_supported(dtype, p->D, bn)) {
     if (verbose()) {
       std::fprintf(stderr, "fa_forward: block_n=%d is not built (0, 32, 64 or 128)\n", bn);

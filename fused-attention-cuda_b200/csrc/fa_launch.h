@@ -28,7 +28,7 @@ struct LaunchArgs {
 
 // Which key-tile widths this build instantiates for (dtype, D).
 bool block_n_supported(int dtype, int D, int block_n);
-int default_block_n(int dtype, int D, int N);
+int default_block_n(int dtype, int D, int N, int causal);
 
 // Workspace of the fp32 path: tf32-rounded copies of q, k and v.
 size_t workspace_bytes_f32(int B, int H, int Hkv, int N, int D);

@@ -35,15 +35,16 @@ KV_EMPTY_BIT = 1 << 6
 TOL = {torch.float16: (2e-3, 1e-3), torch.bfloat16: (8e-3, 1e-3), torch.float32: (5e-3, 2e-3)}
 
 
-@pytest.mark.parametrize("d,dtype", [(64, torch.float16), (128, torch.float16),
-                                     (128, torch.bfloat16), (64, torch.float32)],
-                         ids=["d64-fp16", "d128-fp16-lookahead", "d128-bf16-lookahead",
-                              "d64-fp32-tf32"])
-def test_bounded_wait_runs_out_and_context_survives(d, dtype, make_qkv, restore_knobs):
-    """Each kernel the dispatcher picks by default (the 128-key kernel at D=64, the lookahead
-    kernel at D=128, the tf32 path for fp32).  Which bounded wait runs out first depends on
-    timing: the MMA issuer's wait for the missing K tile (kStKFull) or the producer's wait for
-    the ring slot that tile never frees (kStKVEmpty)."""
+@pytest.mark.parametrize("d,dtype,causal", [(64, torch.float16, False), (64, torch.float16, True),
+                                            (128, torch.float16, False), (128, torch.bfloat16, False),
+                                            (64, torch.float32, False)],
+                         ids=["d64-fp16", "d64-fp16-causal-lookahead", "d128-fp16-lookahead",
+                              "d128-bf16-lookahead", "d64-fp32-tf32"])
+def test_bounded_wait_runs_out_and_context_survives(d, dtype, causal, make_qkv, restore_knobs):
+    """Each kernel the dispatcher picks by default (the 128-key kernel at D=64 except fp16
+    causal, the lookahead kernel at D=128 and for fp16 causal D=64, the tf32 path for fp32).
+    Which bounded wait runs out first depends on timing: the MMA issuer's wait for the missing K
+    tile (kStKFull) or the producer's wait for the ring slot that tile never frees (kStKVEmpty)."""
     stage = 3 if dtype == torch.float32 else 5
     if not fused_attn.is_available() or not fused_attn.impl_supports(stage, dtype, d):
         pytest.skip("kernel not available")
@@ -52,7 +53,7 @@ def test_bounded_wait_runs_out_and_context_survives(d, dtype, make_qkv, restore_
 
     fused_attn.set_wait_timeout_ns(100_000_000)
     fused_attn.debug_set_skip_kv_tile(1)
-    fused_attn.forward(q, k, v, is_causal=False)
+    fused_attn.forward(q, k, v, is_causal=causal)
     err, bits = fused_attn.last_device_error()  # synchronises: the launch has ended
     assert err == LAUNCH_TIMEOUT
     assert bits & (K_FULL_BIT | KV_EMPTY_BIT), f"cause bits {bits:#x}"
@@ -60,9 +61,9 @@ def test_bounded_wait_runs_out_and_context_survives(d, dtype, make_qkv, restore_
 
     fused_attn.debug_set_skip_kv_tile(-1)
     fused_attn.set_wait_timeout_ns(2_000_000_000)
-    o, lse = fused_attn.forward(q, k, v, is_causal=False, return_lse=True)
+    o, lse = fused_attn.forward(q, k, v, is_causal=causal, return_lse=True)
     torch.cuda.synchronize()
     assert fused_attn.last_device_error() == (0, 0)
-    o_ref, lse_ref = oracle.attention(q, k, v, threads=oracle.default_threads())
+    o_ref, lse_ref = oracle.attention(q, k, v, causal=causal, threads=oracle.default_threads())
     tol_o, tol_l = TOL[dtype]
     assert oracle.max_abs(o, o_ref) <= tol_o and oracle.max_abs(lse, lse_ref) <= tol_l
