@@ -163,10 +163,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int G = static_cast<int>(gridDim.x);
   const int cta = static_cast<int>(blockIdx.x);
 
+  int pre_k = 0;  // K tiles of the first item issued in the prologue (thread 0 only)
   if (threadIdx.x == 0) {
 #ifdef FA_TRACE
     if (blockIdx.x < kTraceCtas) g_trace_t0[blockIdx.x] = clock64();
 #endif
+    tma_prefetch_desc(&tm_q);
+    tma_prefetch_desc(&tm_k);
     mbar_init(bar(L::kBarQFull), 1);
     mbar_init(bar(L::kBarQEmpty), 1);
     for (int g = 0; g < 2; ++g) {
@@ -187,6 +190,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     *abort_flag = 0;
     fence_mbar_init();
+    // Thread 0 is also the Q/K producer: the first item's Q and first K tiles go out now, ahead of
+    // the tensor-memory allocation and the CTA barrier (at a cold start they come from DRAM, and
+    // the first S waits for them); the producer loop skips them.
+    const Item it0 = decode_item<CAUSAL>(item_index(0, G, cta), args);
+    const Heads hd0 = split_heads(it0.bh, args);
+    const int kv_end0 = CAUSAL ? min(args.N, it0.q_tile * kBlockM + kBlockM) : args.N;
+    mbar_arrive_expect_tx(bar(L::kBarQFull), L::kQBytes);
+#pragma unroll
+    for (int c = 0; c < L::kDChunks; ++c) {
+      tma_load_view(sbase + L::kQOff + c * L::kQChunkBytes, &tm_q, c * L::kSwElems,
+                    it0.q_tile * kBlockM, hd0.h, hd0.b, args.q_pos, bar(L::kBarQFull));
+    }
+    pre_k = min(KST, (kv_end0 + BN - 1) / BN);
+    for (int j = 0; j < pre_k; ++j) {
+      if (j == args.skip_kv_tile) continue;
+      mbar_arrive_expect_tx(bar(L::kBarKFull + j), L::kKVBytes);
+#pragma unroll
+      for (int c = 0; c < L::kDChunks; ++c) {
+        tma_load_view(sbase + L::kKOff + j * L::kKVBytes + c * L::kKVChunkBytes, &tm_k,
+                      c * L::kSwElems, j * BN, hd0.hk, hd0.b, args.k_pos, bar(L::kBarKFull + j));
+      }
+    }
   }
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
@@ -209,8 +234,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int bar_empty = is_k ? L::kBarKEmpty : L::kBarVEmpty;
       const uint32_t ring = sbase + (is_k ? L::kKOff : L::kVOff);
       const CUtensorMap* tm = is_k ? &tm_k : &tm_v;
-      if (is_k) tma_prefetch_desc(&tm_q);
-      tma_prefetch_desc(tm);
+      if (!is_k) tma_prefetch_desc(tm);
       int count = 0;        // tiles this producer has issued, over all items
       int items_done = 0;   // items whose Q this producer loaded (warp 0)
       unsigned skipped = 0;  // bit (count % 32): that tile's copy was skipped (fault injection)
@@ -230,11 +254,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                                   w, kStKVEmpty))) {
             break;
           }
-          mbar_arrive_expect_tx(bar(L::kBarQFull), L::kQBytes);
+          if (items_done > 0) {  // the first item's Q went out in the prologue
+            mbar_arrive_expect_tx(bar(L::kBarQFull), L::kQBytes);
 #pragma unroll
-          for (int c = 0; c < L::kDChunks; ++c) {
-            tma_load_view(sbase + L::kQOff + c * L::kQChunkBytes, &tm_q, c * L::kSwElems, q0,
-                          hd.h, hd.b, args.q_pos, bar(L::kBarQFull));
+            for (int c = 0; c < L::kDChunks; ++c) {
+              tma_load_view(sbase + L::kQOff + c * L::kQChunkBytes, &tm_q, c * L::kSwElems, q0,
+                            hd.h, hd.b, args.q_pos, bar(L::kBarQFull));
+            }
           }
           ++items_done;
         }
@@ -249,6 +275,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             continue;
           }
           skipped &= ~(1u << (count & 31));
+          if (is_k && r == 0 && j < pre_k) continue;  // issued in the prologue
           mbar_arrive_expect_tx(bar(bar_full + s), L::kKVBytes);
 #pragma unroll
           for (int c = 0; c < L::kDChunks; ++c) {
