@@ -273,6 +273,24 @@ def test_causal_equals_explicit_tril_mask(dtype, make_qkv):
     assert torch.equal(o[:, :, 0, :], v[:, :, 0, :])
 
 
+@pytest.mark.parametrize("bn", [0, 64, 128], ids=["default", "lookahead", "kt128"])
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+@pytest.mark.parametrize("d", [64, 128])
+@pytest.mark.parametrize("dtype", DTYPES, ids=dtype_id)
+def test_running_max_jumps_in_late_key_tiles(dtype, d, causal, bn, make_qkv, reset_overrides):
+    """Keys whose scores jump far above every earlier score of their rows (a query-aligned key
+    scaled by 6) in the third and fifth key tiles: the running max of those rows rises by far more
+    than the lazy-rescale threshold mid-item, so the O correction of a later tile runs (fp16's
+    lazy path and bf16's eager one), in every kernel."""
+    require(dtype, d)
+    q, k, v = make_qkv(1, 2, 640, d, dtype=dtype, device="cuda", seed=19)
+    for pos in (300, 531):
+        k[:, :, pos, :] = q[:, :, pos + 7, :] * 6
+    fused_attn.set_debug_overrides(0, bn)
+    o, lse = fused_attn.forward_stage(q, k, v, 5, is_causal=causal)
+    check(o, lse, q, k, v, causal, dtype)
+
+
 @pytest.mark.parametrize("scale", [0.05, 0.25])
 @pytest.mark.parametrize("dtype", DTYPES, ids=dtype_id)
 def test_non_default_scale(dtype, scale, make_qkv):
