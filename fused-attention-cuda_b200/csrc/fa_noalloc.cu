@@ -1,7 +1,10 @@
 // fa_noalloc.cu -- fa_forward without a caller-provided workspace: the scratch the fp32 path
 // needs (tf32-rounded copies of q, k, v) comes from a fixed device array compiled into this
-// library, so the call performs no allocation of any kind.  fp16/bf16 need no scratch and go
-// straight to fa_forward.
+// library, so the call performs no allocation of any kind.  It is for callers that cannot
+// allocate device memory when they call: a host function enqueued on a stream may make no CUDA
+// API calls at all, some runtimes reserve all device memory up front and hand a plugin no
+// allocator, and latency-critical loops avoid cudaMalloc/cudaFree because they can synchronize
+// the device.  fp16/bf16 need no scratch and go straight to fa_forward.
 //
 // The scratch is one array per device context, shared by every call: two calls whose lifetimes
 // overlap on the device (different streams, or different host threads) race on it.  Its device

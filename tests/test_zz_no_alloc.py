@@ -1,5 +1,9 @@
 """fa_forward_noalloc: the forward with scratch from the library's fixed device array.
 
+For callers that cannot allocate device memory when they call (a host function enqueued on a
+stream may make no CUDA API calls; some runtimes reserve all device memory up front and give a
+plugin no allocator): the fp32 path's 64 MiB of scratch lives in the library, not in a workspace.
+
 Collected last (file name) but independent of the other tests: every case compares the
 no-allocation entry point with fa_forward given an explicit workspace, on two calls in a row
 (the second call reuses the scratch the first one left behind).
