@@ -54,10 +54,12 @@
 // is carried as P_hi + P_lo (both bf16, the second half of S_w holds P_lo) and multiplied twice.
 // Every other row averages >= 128 keys and its rounding errors average out.
 
-// O rescaling is lazy: the max used for the exponent (m_ref) only moves when the tile max
-// exceeds it by more than 2^8 in exponent units, so P stays <= 256 (exact in fp16/bf16 range)
-// and the O read-modify-write through TMEM is rare.  The final o = acc/l and lse use the same
-// m_ref, so the result is the same function (FlashAttention-4's conditional rescaling).
+// O rescaling is lazy for fp16 and tf32: the max used for the exponent (m_ref) only moves when the
+// tile max exceeds it by more than 2^8 in exponent units, so P stays <= 256 (in range) and the O
+// read-modify-write through TMEM is rare.  The final o = acc/l and lse use the same m_ref, so the
+// result is the same function (FlashAttention-4's conditional rescaling).  bf16 rescales whenever
+// the max grows: with 8 significant bits, a weight above 1 that dominates its row would carry
+// its rounding error straight into O.
 //
 // Every mbarrier wait is bounded (globaltimer); a wait that runs out sets a CTA-local abort flag,
 // records a cause bit in g_status and the launch epoch in g_abort_epoch (so other CTAs of the
@@ -149,6 +151,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   using L = Layout<static_cast<int>(sizeof(T)), D, BN, KST, VST>;
   constexpr bool kTf32 = std::is_same<T, float>::value;
   constexpr uint32_t kFmt = std::is_same<T, __nv_bfloat16>::value ? 1u : (kTf32 ? 2u : 0u);
+  // Rescale threshold (log2 units).  fp16 P and tf32 P keep 11 significant bits, so weights up to
+  // 2^8 (lazy rescaling) cost nothing; bf16 keeps 8, and a row dominated by one key must keep its
+  // largest weight exactly 1 (rescale whenever the running max grows), or that weight's rounding
+  // alone moves O past the 8e-3 gate.
+  constexpr float kResc = std::is_same<T, __nv_bfloat16>::value ? 0.0f : kRescaleThreshold;
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -473,7 +480,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const float m_new = fmaxf(m_ref, row_max<BN>(s));
         const bool resc = (m_ref == -INFINITY) ? (m_new != -INFINITY)
-                                               : ((m_new - m_ref) * sl2 > kRescaleThreshold);
+                                               : ((m_new - m_ref) * sl2 > kResc);
         const float m_use = resc ? m_new : m_ref;
         const float alpha =
             resc ? ((m_ref == -INFINITY) ? 0.f : ex2_approx((m_ref - m_use) * sl2)) : 1.f;
