@@ -920,16 +920,17 @@ bool block_n_supported(int dtype, int D, int block_n) {
 }
 
 // Default key-tile choice: the lookahead kernel (128-key rounds split 64/64 between the softmax
-// warpgroups, selected by block_n = 64) for D = 128 and for fp16 causal at D = 64; the 128-key
-// kernel for the rest of D = 64, where the lookahead kernel's per-round overheads weigh more
-// against the shorter MMAs.  Measured on B200 (TFLOP/s, 128-key / lookahead): fp16 causal D=64
-// B8H32 N512-4096 175/199 .. 550/562, the GPT-2 block's B16H12 N1024 300/331, C2c 280/299,
-// N=8192 604/599; fp16 full D=64 C2 400/399, B8H32 N2048 607/607; bf16 causal D=64 C2c
-// 277/262.  fp32 runs 64-key tf32 tiles.
+// warpgroups, selected by block_n = 64) for D = 128 and for causal attention at D = 64; the
+// 128-key kernel for full attention at D = 64, where the lookahead kernel's per-round overheads
+// weigh more against the shorter MMAs.  Measured on B200 (TFLOP/s, 128-key / lookahead): fp16
+// causal D=64 B8H32 N512-4096 175/199 .. 550/562, the GPT-2 block's B16H12 N1024 300/331, C2c
+// 280/299, N=8192 604/599; bf16 causal D=64 B8H32 N2048 381/408, B16H12 N1024 260/292, C2c
+// 261/262; fp16 full D=64 C2 400/399, B8H32 N2048 607/607; bf16 full D=64 C2 399/380, B8H32
+// N2048 575/548.  fp32 runs 64-key tf32 tiles.
 int default_block_n(int dtype, int D, int /*N*/, int causal) {
   if (dtype == FA_DTYPE_F32) return 64;
   if (D == 128) return 64;
-  return (dtype == FA_DTYPE_F16 && causal) ? 64 : 128;
+  return causal ? 64 : 128;
 }
 
 cudaError_t launch_forward(const LaunchArgs& a, cudaStream_t stream) {

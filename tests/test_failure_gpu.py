@@ -41,8 +41,8 @@ TOL = {torch.float16: (2e-3, 1e-3), torch.bfloat16: (8e-3, 1e-3), torch.float32:
                          ids=["d64-fp16", "d64-fp16-causal-lookahead", "d128-fp16-lookahead",
                               "d128-bf16-lookahead", "d64-fp32-tf32"])
 def test_bounded_wait_runs_out_and_context_survives(d, dtype, causal, make_qkv, restore_knobs):
-    """Each kernel the dispatcher picks by default (the 128-key kernel at D=64 except fp16
-    causal, the lookahead kernel at D=128 and for fp16 causal D=64, the tf32 path for fp32).
+    """Each kernel the dispatcher picks by default (the 128-key kernel for full attention at
+    D=64, the lookahead kernel at D=128 and for causal D=64, the tf32 path for fp32).
     Which bounded wait runs out first depends on timing: the MMA issuer's wait for the missing K
     tile (kStKFull) or the producer's wait for the ring slot that tile never frees (kStKVEmpty)."""
     stage = 3 if dtype == torch.float32 else 5
