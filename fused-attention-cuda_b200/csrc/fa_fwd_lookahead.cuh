@@ -655,11 +655,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(bar(L::kBarPFull + g));
       }
       // ---- merge the two partials; O / l staged in shared memory and written by TMA; LSE ----
-      if (ok) {  // the item's last PV round
-        ok = __all_sync(0xffffffffu, wait_bounded(bar(L::kBarPVDone + g),
-                                                  static_cast<uint32_t>(pvc) & 1u, w, kStODone));
-        ++pvc;
-      }
       // The previous item's O store must have read the staging buffer (the exchange lives there).
       if (o_issuer) bulk_wait_read();
       tc_fence_before();
@@ -681,6 +676,18 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool in_range = row < args.N;
       // Every thread has read the exchange before O overwrites it.
       named_barrier_sync(kMergeBarrier, 2 * kBlockM);
+      // The item's last PVs: waited for only now, so that the exchange above runs under them.  A
+      // wait that runs out here does not leave the epilogue (every thread still reaches its
+      // named barriers); the abort flag it sets ends the next item's first wait.
+      if (ok) {
+        ok = __all_sync(0xffffffffu, wait_bounded(bar(L::kBarPVDone + g),
+                                                  static_cast<uint32_t>(pvc) & 1u, w, kStODone));
+        ++pvc;
+      }
+      // Each warpgroup reads both accumulators: both groups' last PVs must be complete.
+      tc_fence_before();
+      named_barrier_sync(kMergeBarrier, 2 * kBlockM);
+      tc_fence_after();
       // Each warpgroup normalises half of the head dimension into the staging buffer: row r of
       // 64-column chunk c at kOStOff + c*16 KB + r*128 B, 16-byte units XOR-swizzled by r % 8 (the
       // layout of the O tensor map's 128-byte swizzle).
