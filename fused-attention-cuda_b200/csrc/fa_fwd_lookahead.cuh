@@ -674,8 +674,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
       const float f0 = a0 * inv_l, f1 = a1 * inv_l;
       const bool in_range = row < args.N;
-      // Every thread has read the exchange before O overwrites it.
-      named_barrier_sync(kMergeBarrier, 2 * kBlockM);
+      if (g == 0 && in_range) {
+        args.lse[static_cast<size_t>(item.bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)] =
+            (l > 0.f && m != -INFINITY) ? fmaf(m, args.scale, logf(l)) : INFINITY;
+      }
       // The item's last PVs: waited for only now, so that the exchange above runs under them.  A
       // wait that runs out here does not leave the epilogue (every thread still reaches its
       // named barriers); the abort flag it sets ends the next item's first wait.
@@ -684,7 +686,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                   static_cast<uint32_t>(pvc) & 1u, w, kStODone));
         ++pvc;
       }
-      // Each warpgroup reads both accumulators: both groups' last PVs must be complete.
+      // Each warpgroup reads both accumulators: both groups' last PVs must be complete.  (The same
+      // barrier orders every thread's exchange reads before O overwrites the exchange.)
       tc_fence_before();
       named_barrier_sync(kMergeBarrier, 2 * kBlockM);
       tc_fence_after();
@@ -694,8 +697,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int c = g * (D / 2); c < (g + 1) * (D / 2); c += 32) {
         uint32_t u0[32], u1[32];
-        tmem_ld32_wait(tl + L::kColO + c, u0);
-        tmem_ld32_wait(tl + L::kColO + D + c, u1);
+        tmem_ld32_nowait(tl + L::kColO + c, u0);
+        tmem_ld32_nowait(tl + L::kColO + D + c, u1);
+        tmem_wait_ld_regs(u0);
+        tmem_wait_ld_regs(u1);
         float o[32];
 #pragma unroll
         for (int k2 = 0; k2 < 32; ++k2) {
@@ -715,10 +720,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       // O_0 and O_1 have been read: the next item's first PVs may overwrite them.
       tc_fence_before();
       mbar_arrive(bar(L::kBarOFree));
-      if (g == 0 && in_range) {
-        args.lse[static_cast<size_t>(item.bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)] =
-            (l > 0.f && m != -INFINITY) ? fmaf(m, args.scale, logf(l)) : INFINITY;
-      }
       // The staged tile goes out in one TMA store per 64-column chunk (rows past N are clipped);
       // it overlaps the next item.
       fence_proxy_async_smem();
