@@ -635,13 +635,21 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++pvc;
           tc_fence_after();
           if (__any_sync(0xffffffffu, resc)) {
+            // 64 columns per wait: two loads in flight, then both scaled and stored back.
 #pragma unroll
-            for (int c = 0; c < D; c += 32) {
-              uint32_t u[32];
-              tmem_ld32_wait(tl + o_col + c, u);
+            for (int c = 0; c < D; c += 64) {
+              uint32_t u[32], v[32];
+              tmem_ld32_nowait(tl + o_col + c, u);
+              tmem_ld32_nowait(tl + o_col + c + 32, v);
+              tmem_wait_ld_regs(u);
+              tmem_wait_ld_regs(v);
 #pragma unroll
-              for (int k2 = 0; k2 < 32; ++k2) u[k2] = __float_as_uint(__uint_as_float(u[k2]) * alpha);
+              for (int k2 = 0; k2 < 32; ++k2) {
+                u[k2] = __float_as_uint(__uint_as_float(u[k2]) * alpha);
+                v[k2] = __float_as_uint(__uint_as_float(v[k2]) * alpha);
+              }
               tmem_st32(tl + o_col + c, u);
+              tmem_st32(tl + o_col + c + 32, v);
             }
           }
         }
