@@ -103,6 +103,11 @@ class ClockSampler:
         self.proc = None
         self.thread = None
         self.t0 = self.t1 = None
+        # NVML read every ~2 ms as well: nvidia-smi's 50 ms period can miss a timed region of a
+        # few milliseconds entirely.  (t, sm MHz, max sm MHz, clocks-event-reason bit mask)
+        self.fast: list[tuple[float, float, float, int]] = []
+        self.fast_stop = threading.Event()
+        self.fast_thread = None
 
     def start(self) -> None:
         try:
@@ -115,6 +120,25 @@ class ClockSampler:
             return
         self.thread = threading.Thread(target=self._read, daemon=True)
         self.thread.start()
+        self.fast_thread = threading.Thread(target=self._poll_nvml, daemon=True)
+        self.fast_thread.start()
+
+    def _poll_nvml(self) -> None:
+        """Read-only NVML queries of the SM clock and the clocks-event reasons."""
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            mx = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            while not self.fast_stop.is_set():
+                sm = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+                why = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+                self.fast.append((time.time(), sm, mx, why))
+                time.sleep(0.002)
+            pynvml.nvmlShutdown()
+        except Exception:  # NVML absent or refused: the nvidia-smi samples stand alone
+            return
 
     def _read(self) -> None:
         for line in self.proc.stdout:
@@ -145,7 +169,20 @@ class ClockSampler:
             self.proc.kill()
         if self.thread:
             self.thread.join(timeout=2)
+        self.fast_stop.set()
+        if self.fast_thread:
+            self.fast_thread.join(timeout=2)
         inside = [s for t, s in self.samples if self.t0 is not None and self.t0 <= t <= self.t1]
+        fast_in = [f for f in self.fast if self.t0 is not None and self.t0 <= f[0] <= self.t1]
+        if not inside and fast_in:
+            bits = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+                    "sw_power_cap": 0x4}
+            reasons = sorted(n for n, b in bits.items() if any(f[3] & b for f in fast_in))
+            return {"sm_mhz": statistics.median(f[1] for f in fast_in),
+                    "sm_max_mhz": max(f[2] for f in fast_in), "reasons": reasons,
+                    "samples": len(fast_in), "samples_in_timed_region": len(fast_in),
+                    "source": "NVML every ~2 ms (the timed region is shorter than nvidia-smi's "
+                              "50 ms period)"}
         use = inside or [s for _, s in self.samples]
         sm, mx, reasons = [], [], set()
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]

@@ -79,3 +79,24 @@ def test_committed_sweep_is_sane_and_its_table_is_current():
     assert benchcsv.validate(header, rows, roof_tflops=roof) == []
     assert {r["impl"] for r in rows} >= {"tuned"}
     assert SWEEP.with_suffix(".md").read_text() == benchcsv.to_markdown(rows)
+
+
+def test_clock_record_falls_back_to_fast_nvml_samples():
+    """A timed region shorter than nvidia-smi's 50 ms period gets no nvidia-smi sample; the clock
+    record then comes from the ~2 ms NVML samples inside the region (median SM clock, union of
+    the throttle reasons seen)."""
+    import bench
+
+    c = bench.ClockSampler(0)
+    # stop() only needs a process handle that can be terminated
+    c.proc = type("P", (), {"terminate": lambda self: None, "wait": lambda self, timeout=None: 0})()
+    c.samples = [(0.0, ["0", "1965", "1965", "300", "0x0", "Not Active", "Not Active",
+                        "Not Active", "Not Active"])]
+    c.fast = [(10.001, 1965.0, 1965.0, 0x0), (10.003, 1950.0, 1965.0, 0x4),
+              (10.005, 1965.0, 1965.0, 0x0), (11.0, 900.0, 1965.0, 0x8)]
+    c.window(10.0, 10.01)
+    rec = c.stop()
+    assert rec["samples_in_timed_region"] == 3
+    assert rec["sm_mhz"] == 1965.0 and rec["sm_max_mhz"] == 1965.0
+    assert rec["reasons"] == ["sw_power_cap"]
+    assert "NVML" in rec["source"]
