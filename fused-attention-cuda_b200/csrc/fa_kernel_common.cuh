@@ -166,9 +166,11 @@ __device__ __forceinline__ void wait_drain(uint32_t bar, uint32_t parity,
 }
 
 // Every kEmuEvery-th pair of exponentials goes to the FMA pipes (ex2_poly3) instead of the MUFU
-// unit; 0 keeps them all on MUFU.  Set at build time with -DFA_EX2_EMU_EVERY=n.
+// unit; 0 keeps them all on MUFU.  Set at build time with -DFA_EX2_EMU_EVERY=n.  One pair in eight
+// measured best for the 128-key kernel (the D=64 full-attention default): B2H8 N8192 D64 664 ->
+// 692 TFLOP/s, B8H32 N2048 608 -> 620, C2 418 -> 419; one in six or four is slower.
 #ifndef FA_EX2_EMU_EVERY
-#define FA_EX2_EMU_EVERY 0
+#define FA_EX2_EMU_EVERY 8
 #endif
 constexpr int kEmuEvery = FA_EX2_EMU_EVERY;
 
