@@ -273,6 +273,34 @@ def test_causal_equals_explicit_tril_mask(dtype, make_qkv):
     assert torch.equal(o[:, :, 0, :], v[:, :, 0, :])
 
 
+@pytest.mark.parametrize("bn", [64, 128], ids=["lookahead", "kt128"])
+@pytest.mark.parametrize("n", [128, 160])
+@pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+@pytest.mark.parametrize("dtype", DTYPES, ids=dtype_id)
+def test_many_short_items_per_cta(dtype, causal, n, bn, make_qkv, reset_overrides):
+    """768 / 1536 one- or two-round items on 148 CTAs: five to eleven item epilogues per CTA back
+    to back, so the exchange and O staging buffers, the O_free hand-off and the first item's loads
+    issued from the prologue are all exercised many times per CTA (N=160 adds a ragged tile)."""
+    require(dtype, 64)
+    q, k, v = make_qkv(16, 48, n, 64, dtype=dtype, device="cuda", seed=23)
+    fused_attn.set_debug_overrides(0, bn)
+    o, lse = fused_attn.forward_stage(q, k, v, 5, is_causal=causal)
+    o_ref, lse_ref = oracle.attention(q, k, v, causal=causal, threads=THREADS)
+    assert oracle.max_abs(lse, lse_ref) <= TOL_LSE[dtype]
+    # Over 768 heads some causal rows average only 1-3 keys and reach |O| >= 4, where a single
+    # bf16 rounding of the exact result is already up to 2^-6 = 1.56e-2 (PyTorch's own bf16
+    # attention misses by 1.7e-2 on these inputs).  So each element must meet the dtype's gate or,
+    # where larger, half a unit in the last place of its reference value in the output dtype plus
+    # 2e-3.
+    ref = np.asarray(o_ref, dtype=np.float64)
+    err = np.abs(o.float().cpu().numpy().astype(np.float64) - ref)
+    mant = 7 if dtype == torch.bfloat16 else 10
+    half_ulp = 0.5 * np.exp2(np.floor(np.log2(np.maximum(np.abs(ref), 1e-30))) - mant)
+    bound = np.maximum(TOL_O[dtype], half_ulp + 2e-3)
+    worst = float((err - bound).max())
+    assert worst <= 0.0, f"max excess over the bound {worst:.3e} (max|dO| {err.max():.3e})"
+
+
 @pytest.mark.parametrize("bn", [0, 64, 128], ids=["default", "lookahead", "kt128"])
 @pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
 @pytest.mark.parametrize("d", [64, 128])
