@@ -276,13 +276,14 @@ def test_causal_equals_explicit_tril_mask(dtype, make_qkv):
 @pytest.mark.parametrize("bn", [64, 128], ids=["lookahead", "kt128"])
 @pytest.mark.parametrize("n", [128, 160])
 @pytest.mark.parametrize("causal", [False, True], ids=["full", "causal"])
+@pytest.mark.parametrize("d", [64, 128])
 @pytest.mark.parametrize("dtype", DTYPES, ids=dtype_id)
-def test_many_short_items_per_cta(dtype, causal, n, bn, make_qkv, reset_overrides):
+def test_many_short_items_per_cta(dtype, d, causal, n, bn, make_qkv, reset_overrides):
     """768 / 1536 one- or two-round items on 148 CTAs: five to eleven item epilogues per CTA back
     to back, so the exchange and O staging buffers, the O_free hand-off and the first item's loads
     issued from the prologue are all exercised many times per CTA (N=160 adds a ragged tile)."""
-    require(dtype, 64)
-    q, k, v = make_qkv(16, 48, n, 64, dtype=dtype, device="cuda", seed=23)
+    require(dtype, d)
+    q, k, v = make_qkv(16, 48, n, d, dtype=dtype, device="cuda", seed=23)
     fused_attn.set_debug_overrides(0, bn)
     o, lse = fused_attn.forward_stage(q, k, v, 5, is_causal=causal)
     o_ref, lse_ref = oracle.attention(q, k, v, causal=causal, threads=THREADS)
