@@ -186,9 +186,15 @@ const char* check_strides(const long long st[3], size_t eb, const char* name) {
   return nullptr;
 }
 
-int forward_impl(int impl, int dtype, const void* q, const void* k, const void* v, void* o,
-                 float* lse, void* workspace, const fa_params_t* p, const fa_strides_t* st,
-                 cudaStream_t stream) {
+}  // namespace
+
+namespace fa_sm100 {
+
+// Every check fa_forward makes before it launches, in its order and with its error codes:
+// parameters, strides (when given), the implementation on the current device, the workspace.
+cudaError_t check_forward_args(int impl, int dtype, const void* q, const void* k, const void* v,
+                               const void* o, const float* lse, const void* workspace,
+                               bool need_workspace, const fa_params_t* p, const fa_strides_t* st) {
   if (const char* why = validate(dtype, q, k, v, o, lse, p)) {
     if (verbose()) std::fprintf(stderr, "fa_forward: invalid params: %s\n", why);
     return cudaErrorInvalidValue;
@@ -216,12 +222,27 @@ int forward_impl(int impl, int dtype, const void* q, const void* k, const void* 
     }
     return cudaErrorNotSupported;
   }
-  if (fa_workspace_bytes(impl, dtype, p) > 0 && (workspace == nullptr || !aligned16(workspace))) {
+  if (need_workspace && fa_workspace_bytes(impl, dtype, p) > 0 &&
+      (workspace == nullptr || !aligned16(workspace))) {
     if (verbose()) {
       std::fprintf(stderr, "fa_forward: workspace must be non-null and 16-byte aligned "
                            "(fa_workspace_bytes > 0)\n");
     }
     return cudaErrorInvalidValue;
+  }
+  return cudaSuccess;
+}
+
+}  // namespace fa_sm100
+
+namespace {
+
+int forward_impl(int impl, int dtype, const void* q, const void* k, const void* v, void* o,
+                 float* lse, void* workspace, const fa_params_t* p, const fa_strides_t* st,
+                 cudaStream_t stream) {
+  if (const cudaError_t e =
+          fa_sm100::check_forward_args(impl, dtype, q, k, v, o, lse, workspace, true, p, st)) {
+    return static_cast<int>(e);
   }
   int bm = 0, bn = 0;
   fa_get_debug_overrides(1, &bm, &bn);

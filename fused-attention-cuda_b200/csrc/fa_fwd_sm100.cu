@@ -808,25 +808,23 @@ cudaError_t prepare(const LaunchArgs& a, int D, int BN, Prepared* pr) {
   return cudaSuccess;
 }
 
-// Opts the kernel into its dynamic shared memory once per device.
+// Opts the kernel into its dynamic shared memory.  Done on every launch: the attribute belongs to
+// the kernel as loaded in the current context, not to the device, so a flag remembered per device
+// would be stale after cudaDeviceReset or for a caller running in a context of its own (a
+// driver-API plugin); the call is a host-side attribute update and allocates nothing.
 template <typename Kern>
-cudaError_t opt_in_smem(Kern* kern, int bytes, std::atomic<unsigned long long>* configured, int dev) {
-  const unsigned long long bit = 1ull << (dev & 63);
-  if ((configured->load(std::memory_order_acquire) & bit) != 0) return cudaSuccess;
-  const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
-  if (e == cudaSuccess) configured->fetch_or(bit, std::memory_order_acq_rel);
-  return e;
+cudaError_t opt_in_smem(Kern* kern, int bytes) {
+  return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
 }
 
 template <typename T, int D, int BN, int KST, int VST, bool CAUSAL>
 cudaError_t launch_impl(const LaunchArgs& a, cudaStream_t stream) {
   using L = Layout<static_cast<int>(sizeof(T)), D, BN, KST, VST>;
   auto* kern = &fa_fwd_sm100_kernel<T, D, BN, KST, VST, CAUSAL>;
-  static std::atomic<unsigned long long> configured{0};
   Prepared pr;
   cudaError_t e = prepare<T>(a, D, BN, &pr);
   if (e != cudaSuccess) return e;
-  if ((e = opt_in_smem(kern, L::kSmemAlloc, &configured, pr.dev)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(kern, L::kSmemAlloc)) != cudaSuccess) return e;
   kern<<<pr.grid, kThreads, L::kSmemAlloc, stream>>>(pr.mq, pr.mk, pr.mv, pr.mo, pr.ka);
   return cudaGetLastError();
 }
@@ -839,11 +837,10 @@ cudaError_t launch_lookahead(const LaunchArgs& a, cudaStream_t stream) {
   constexpr int kVSt = D == 128 ? 2 : 5;
   using L = LaLayout<D, kKSt, kVSt>;
   auto* kern = &fa_fwd_lookahead_kernel<T, D, kKSt, kVSt, CAUSAL, true>;
-  static std::atomic<unsigned long long> configured{0};
   Prepared pr;
   cudaError_t e = prepare<T>(a, D, L::BR, &pr);
   if (e != cudaSuccess) return e;
-  if ((e = opt_in_smem(kern, L::kSmemAlloc, &configured, pr.dev)) != cudaSuccess) return e;
+  if ((e = opt_in_smem(kern, L::kSmemAlloc)) != cudaSuccess) return e;
   kern<<<pr.grid, kThreads, L::kSmemAlloc, stream>>>(pr.mq, pr.mk, pr.mv, pr.mo, pr.ka);
   return cudaGetLastError();
 }

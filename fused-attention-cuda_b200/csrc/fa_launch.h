@@ -6,6 +6,8 @@
 
 #include <cstdint>
 
+#include "fa_sm100.h"
+
 namespace fa_sm100 {
 
 struct LaunchArgs {
@@ -32,6 +34,13 @@ int default_block_n(int dtype, int D, int N, int causal);
 
 // Workspace of the fp32 path: tf32-rounded copies of q, k and v.
 size_t workspace_bytes_f32(int B, int H, int Hkv, int N, int D);
+
+// The checks fa_forward / fa_forward_strided make before launching (st may be null; the
+// workspace is checked only when need_workspace): cudaSuccess, cudaErrorInvalidValue or
+// cudaErrorNotSupported, exactly as those entry points would return them.
+cudaError_t check_forward_args(int impl, int dtype, const void* q, const void* k, const void* v,
+                               const void* o, const float* lse, const void* workspace,
+                               bool need_workspace, const fa_params_t* p, const fa_strides_t* st);
 
 // Validated arguments only; returns the launch status (never synchronises).
 cudaError_t launch_forward(const LaunchArgs& a, cudaStream_t stream);

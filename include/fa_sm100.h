@@ -94,19 +94,21 @@ int fa_forward_strided(int impl, int dtype, const void* q, const void* k, const 
 int fa_combine(int dtype, int n_splits, const void* const* o_parts, const float* const* lse_parts,
                void* o, float* lse, int B, int H, int N, int D, cudaStream_t stream);
 
-/* No counterpart in the reference: fa_forward with no workspace argument and no allocation of
- * any kind, for callers that cannot allocate device memory at call time -- code running in a host
- * function enqueued on a stream (where CUDA forbids CUDA API calls), or inside a runtime that
- * reserves all device memory up front and gives a plugin no allocator -- and for loops that avoid
+/* No counterpart in the reference: fa_forward with no workspace argument and no allocation, for
+ * callers that cannot allocate device memory at call time -- a plugin inside a runtime that
+ * reserves all device memory up front and gives it no allocator -- and for loops that avoid
  * cudaMalloc/cudaFree because those can synchronize the device.  Paths that need scratch (fp32 on
  * FA_IMPL_FUSED: fa_workspace_bytes > 0) use a fixed device array of FA_NOALLOC_SCRATCH_BYTES
- * (64 MiB, held by every GPU that loads the library until the process exits); a problem needing
- * more (e.g. B=8 H=16 N=4096 D=128 fp32, 768 MiB) returns cudaErrorInvalidValue without launching
- * anything.  B=2 H=8 N=2048 D=128 fp32 needs 48 MiB.  That array is shared by all calls on a
- * device and keeps the last call's contents, so calls whose executions overlap on the GPU (other
- * streams or host threads) race on it.  Its device address is looked up on the first call on each
- * device (with that device current), which should therefore come before any stream capture.
- * fp16/bf16 need no scratch and run exactly as fa_forward. */
+ * (64 MiB per CUDA context that uses it, held until the process exits); a problem needing more
+ * (e.g. B=8 H=16 N=4096 D=128 fp32, 768 MiB) returns cudaErrorInvalidValue without launching
+ * anything.  B=2 H=8 N=2048 D=128 fp32 needs 48 MiB.  Invalid or unsupported arguments return the
+ * same codes as fa_forward.  The array is shared by all calls in a context and keeps the last
+ * call's contents, so calls whose executions overlap on the GPU (other streams or host threads)
+ * race on it.  Its address is looked up on each call in the caller's current context; under
+ * CUDA's default lazy module loading the first such call in a context loads the library's module
+ * and so allocates the array once: make that first fp32 call (a tiny one will do) before
+ * reserving the rest of device memory and before any stream capture.  fp16/bf16 need no scratch
+ * and run exactly as fa_forward. */
 #define FA_NOALLOC_SCRATCH_BYTES (64u * 1024u * 1024u)
 int fa_forward_noalloc(int impl, int dtype, const void* q, const void* k, const void* v, void* o,
                        float* lse, const fa_params_t* p, cudaStream_t stream);

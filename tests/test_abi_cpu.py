@@ -9,6 +9,7 @@
 
 from __future__ import annotations
 
+import ctypes
 import re
 import subprocess
 
@@ -129,3 +130,32 @@ def test_null_and_misaligned_pointers_rejected():
 def test_null_params_pointer_rejected():
     err = abi.lib().fa_forward(5, 1, P16, P16, P16, P16, P16, None, None, None)
     assert err == abi.CUDA_ERROR_INVALID_VALUE
+
+
+@pytest.mark.parametrize("case", ["null_params", "d96", "n_ragged", "h_not_multiple", "scale0",
+                                  "misaligned", "null_lse"])
+def test_noalloc_rejects_what_forward_rejects(case):
+    """fa_forward_noalloc makes fa_forward's argument checks, with its codes, before it looks up
+    its scratch array (fp32 on the fused implementation, the only path that uses it)."""
+    good = abi.params(1, 2, 2, 128, 64, 0.125, True)
+    ptr, lse = 256, 512
+    p = good
+    q = ptr
+    if case == "d96":
+        p = abi.params(1, 2, 2, 128, 96, 0.125, True)
+    elif case == "n_ragged":
+        p = abi.params(1, 2, 2, 100, 64, 0.125, True)
+    elif case == "h_not_multiple":
+        p = abi.params(1, 3, 2, 128, 64, 0.125, True)
+    elif case == "scale0":
+        p = abi.params(1, 2, 2, 128, 64, 0.0, True)
+    elif case == "misaligned":
+        q = ptr + 4
+    elif case == "null_lse":
+        lse = 0
+    L = abi.lib()
+    args = (abi.FA_IMPL_FUSED, abi.FA_DTYPE_F32, q, ptr, ptr, ptr, lse or None)
+    pp = None if case == "null_params" else ctypes.byref(p)
+    rc_noalloc = L.fa_forward_noalloc(*args, pp, None)
+    rc_forward = L.fa_forward(*args, None, pp, None)
+    assert rc_noalloc == rc_forward == abi.CUDA_ERROR_INVALID_VALUE

@@ -1,17 +1,21 @@
 """fa_forward_noalloc: the forward with scratch from the library's fixed device array.
 
-For callers that cannot allocate device memory when they call (a host function enqueued on a
-stream may make no CUDA API calls; some runtimes reserve all device memory up front and give a
-plugin no allocator): the fp32 path's 64 MiB of scratch lives in the library, not in a workspace.
+For callers that cannot allocate device memory when they call (a plugin in a runtime that reserves
+all device memory up front and hands it no allocator): the fp32 path's 64 MiB of scratch lives in
+the library, not in a workspace.
 
-Collected last (file name) but independent of the other tests: every case compares the
-no-allocation entry point with fa_forward given an explicit workspace, on two calls in a row
-(the second call reuses the scratch the first one left behind).
+Collected last (file name) and independent of the other tests: every case compares the
+no-allocation entry point with fa_forward given an explicit workspace, on two calls in a row (the
+second call reuses the scratch the first one left behind).  Further cases check that calls after
+the first leave free device memory unchanged, and that a call made in a second CUDA context (one
+a plugin could have created with the driver API) uses that context's array.
 """
 
 from __future__ import annotations
 
 import math
+import subprocess
+import sys
 
 import pytest
 import torch
@@ -87,3 +91,113 @@ def test_problem_beyond_the_scratch_is_rejected():
     ptr = dummy.data_ptr()
     assert abi.forward_noalloc(abi.FA_IMPL_FUSED, abi.FA_DTYPE_F32, ptr, ptr, ptr, ptr, ptr, p) == \
         abi.CUDA_ERROR_INVALID_VALUE
+
+
+def test_calls_after_the_first_allocate_no_device_memory():
+    require()
+    b, h, n, d = 2, 4, 512, 128
+    p = abi.params(b, h, h, n, d, 1.0 / math.sqrt(d), True)
+    stream = torch.cuda.current_stream().cuda_stream
+    inputs = [make_qkv(b, h, n, d, dtype=torch.float32, device="cuda", seed=s) for s in (84, 85)]
+    o, lse = _outputs(inputs[0][0])
+
+    def call(q, k, v):
+        return abi.forward_noalloc(abi.FA_IMPL_FUSED, abi.FA_DTYPE_F32, q.data_ptr(), k.data_ptr(),
+                                   v.data_ptr(), o.data_ptr(), lse.data_ptr(), p, stream)
+
+    assert call(*inputs[0]) == 0  # the first call may load the module (and the array with it)
+    torch.cuda.synchronize()
+    free0, _ = torch.cuda.mem_get_info()
+    used0 = torch.cuda.memory_allocated()
+    for q, k, v in inputs:
+        assert call(q, k, v) == 0
+        torch.cuda.synchronize()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0
+    assert torch.cuda.memory_allocated() == used0
+    assert fused_attn.last_device_error() == (0, 0)
+
+
+# Runs in a fresh process with no torch: the primary context first, then a context created with
+# the driver API (as a plugin might), each with its own buffers; in both, fa_forward_noalloc must
+# equal fa_forward with an explicit workspace, bit for bit.
+_SECOND_CONTEXT = r"""
+import ctypes, importlib.util, math, sys
+import numpy as np
+from cuda.bindings import driver as cu
+
+spec = importlib.util.spec_from_file_location("fa_abi", sys.argv[1])
+abi = importlib.util.module_from_spec(spec)
+spec.loader.exec_module(abi)
+
+def ok(r):
+    err = r[0] if isinstance(r, tuple) else r
+    if err != cu.CUresult.CUDA_SUCCESS:
+        raise SystemExit(f"driver call failed: {err}")
+    return r[1] if isinstance(r, tuple) and len(r) > 1 else None
+
+def run_in_current_context(tag, seed):
+    b, h, n, d = 1, 2, 256, 64
+    p = abi.params(b, h, h, n, d, 1.0 / math.sqrt(d), True)
+    rng = np.random.default_rng(seed)
+    host = [rng.standard_normal((b, h, n, d), dtype=np.float32) for _ in range(3)]
+    nbytes = host[0].nbytes
+    need = int(abi.lib().fa_workspace_bytes(abi.FA_IMPL_FUSED, abi.FA_DTYPE_F32, ctypes.byref(p)))
+    bufs = []
+    def alloc(size):
+        ptr = int(ok(cu.cuMemAlloc(size)))
+        bufs.append(ptr)
+        return ptr
+    q, k, v = (alloc(nbytes) for _ in range(3))
+    for ptr, arr in zip((q, k, v), host):
+        ok(cu.cuMemcpyHtoD(ptr, arr.ctypes.data, nbytes))
+    ws = alloc(need)
+    outs = [(alloc(nbytes), alloc(b * h * n * 4)) for _ in range(3)]
+    assert abi.forward(abi.FA_IMPL_FUSED, abi.FA_DTYPE_F32, q, k, v, outs[0][0], outs[0][1], p,
+                       0, ws) == 0
+    for o, lse in outs[1:]:  # two calls in a row
+        rc = abi.forward_noalloc(abi.FA_IMPL_FUSED, abi.FA_DTYPE_F32, q, k, v, o, lse, p, 0)
+        if rc != 0:
+            raise SystemExit(f"{tag}: fa_forward_noalloc returned {rc}")
+    ok(cu.cuCtxSynchronize())
+    got = []
+    for o, lse in outs:
+        ho = np.empty((b, h, n, d), np.float32)
+        hl = np.empty((b, h, n), np.float32)
+        ok(cu.cuMemcpyDtoH(ho.ctypes.data, o, ho.nbytes))
+        ok(cu.cuMemcpyDtoH(hl.ctypes.data, lse, hl.nbytes))
+        got.append((ho, hl))
+    for ptr in bufs:
+        ok(cu.cuMemFree(ptr))
+    detail = ctypes.c_uint(0)
+    status = abi.lib().fa_last_device_error(ctypes.byref(detail))
+    if status != 0:
+        raise SystemExit(f"{tag}: device status {status} ({detail.value:#x})")
+    ref_o, ref_l = got[0]
+    if not np.isfinite(ref_o).all():
+        raise SystemExit(f"{tag}: workspace path produced non-finite output")
+    for o_, l_ in got[1:]:
+        if not (np.array_equal(o_, ref_o) and np.array_equal(l_, ref_l)):
+            raise SystemExit(f"{tag}: noalloc output differs from the workspace path")
+    print(tag, "ok")
+
+ok(cu.cuInit(0))
+dev = ok(cu.cuDeviceGet(0))
+primary = ok(cu.cuDevicePrimaryCtxRetain(dev))
+ok(cu.cuCtxPushCurrent(primary))
+run_in_current_context("primary", 86)
+ok(cu.cuCtxPopCurrent())
+ctx = ok(cu.cuCtxCreate(0, dev))  # created current
+run_in_current_context("second", 87)
+ok(cu.cuCtxDestroy(ctx))
+ok(cu.cuDevicePrimaryCtxRelease(dev))
+"""
+
+
+def test_second_context_uses_its_own_array():
+    require()
+    pytest.importorskip("cuda.bindings.driver")
+    r = subprocess.run([sys.executable, "-c", _SECOND_CONTEXT, str(abi.LIB_PATH.parent / "abi.py")],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "primary ok" in r.stdout and "second ok" in r.stdout
