@@ -7,10 +7,12 @@ oracle run on the very (rounded) inputs the kernel saw:
     bf16: max|O - O_ref| <= 8e-3 and max|LSE - LSE_ref| <= 1e-3
 
 plus the reference's secondary FlashAttention ratio rule (error <= 2x PyTorch's own unfused
-attention in the same dtype + 1e-6) and its absolute caps.  Configs too large for the oracle in
-seconds (N >= 4096) are checked on sampled rows (first, middle and last query tiles of the first
-and last heads, as the reference's fa_bench self-check does) and, over the whole tensor, against
-PyTorch's fp32 SDPA on the GPU.
+attention in the same dtype + 1e-6) and its absolute caps.  Every BASELINE configuration is
+checked over the whole tensor against the oracle, the C3 sweep up to N=8192 included; C4 (32
+heads of N=16384) over two whole heads, sampled rows of others (as the reference's fa_bench
+self-check samples tiles), and the whole tensor against PyTorch's fp32 SDPA as an extra opinion.
+Head-sharded runs (what each GPU of the multi-GPU configuration computes) must equal the
+one-launch result bit for bit.
 """
 
 from __future__ import annotations
@@ -155,24 +157,47 @@ def test_c3_sequence_sweep(n, dtype, make_qkv):
     require(dtype, 128)
     q, k, v = make_qkv(2, 8, n, 128, dtype=dtype, device="cuda", seed=2)
     o, lse = fused_attn.forward(q, k, v, is_causal=True, return_lse=True)
-    if n <= 1024:
-        check(o, lse, q, k, v, True, dtype, ratio=False)
-    else:
-        check_rows(o, lse, q, k, v, True, dtype, sample_blocks(2, 8, n))
+    # The whole tensor against the oracle at every N (N=8192: ~9 s of fp64 on 16 host threads).
+    check(o, lse, q, k, v, True, dtype, ratio=False)
+    if n >= 4096:
         check_vs_sdpa_fp32(o, q, k, v, True, dtype)
 
 
-def test_c4_long_context_rows(make_qkv):
-    """C4 (B1 H32 N16384 D128 bf16 causal, seed 3) on one GPU: sampled rows vs the oracle and
-    the whole tensor vs fp32 SDPA."""
+def test_c4_long_context(make_qkv):
+    """C4 (B1 H32 N16384 D128 bf16 causal, seed 3) on one GPU: two whole heads (the first and
+    the last) against the oracle, sampled rows of two more, and the whole tensor against fp32
+    SDPA."""
     cfg = CONFIGS["C4"]
     require(cfg.dtype, cfg.D)
     q, k, v = make_qkv(cfg.B, cfg.H, cfg.N, cfg.D, dtype=cfg.dtype, device="cuda", seed=cfg.seed)
     o, lse = fused_attn.forward(q, k, v, is_causal=True, return_lse=True)
     assert bool(torch.isfinite(o).all()) and bool(torch.isfinite(lse).all())
-    blocks = [(0, 0, 0, 64), (0, 0, cfg.N - 64, 64), (0, 31, cfg.N // 2, 64), (0, 17, cfg.N - 32, 32)]
+    for h in (0, cfg.H - 1):
+        sl = slice(h, h + 1)
+        check(o[:, sl].contiguous(), lse[:, sl].contiguous(), q[:, sl].contiguous(),
+              k[:, sl].contiguous(), v[:, sl].contiguous(), True, cfg.dtype, ratio=False)
+    blocks = [(0, 17, cfg.N // 2, 64), (0, 9, cfg.N - 32, 32)]
     check_rows(o, lse, q, k, v, True, cfg.dtype, blocks)
     check_vs_sdpa_fp32(o, q, k, v, True, cfg.dtype)
+
+
+@pytest.mark.parametrize("ranks", [2, 4, 8])
+def test_head_shards_equal_one_launch_bitwise(ranks, make_qkv):
+    """What each GPU of the head-sharded configuration computes (a contiguous block of H/ranks
+    heads, as fused_attn.sharding assigns them) equals the same heads of one launch over all
+    heads, bit for bit: a head's result does not depend on which other heads share the launch
+    or on how the persistent CTAs were dealt the work."""
+    from fused_attn import sharding
+
+    require(torch.bfloat16, 128)
+    b, h, n, d = 1, 32, 2048, 128
+    q, k, v = make_qkv(b, h, n, d, dtype=torch.bfloat16, device="cuda", seed=3)
+    o, lse = fused_attn.forward(q, k, v, is_causal=True, return_lse=True)
+    for r in range(ranks):
+        h0, h1 = sharding.head_range(h, ranks, r)
+        qs, ks, vs = (t[:, h0:h1].contiguous() for t in (q, k, v))
+        o_r, lse_r = fused_attn.forward(qs, ks, vs, is_causal=True, return_lse=True)
+        assert torch.equal(o_r, o[:, h0:h1]) and torch.equal(lse_r, lse[:, h0:h1]), r
 
 
 # ------------------------------------------------------------------------------------------
