@@ -24,12 +24,18 @@ generator).  Default workload: C3 = B2 H8 N2048 D128 fp16 top-left causal, seed 
 Multi-GPU (``torchrun --nproc-per-node N bench.py --gpus N``): one process per GPU, weak scaling:
 rank r runs the same per-GPU workload on its own shard of a global batch of N x B (seed + r), no
 collective on the data path; NCCL only reduces the per-rank device time (max) off the hot path.
-``--workload C4`` instead splits C4's 32 heads of one N=16384 sequence across the ranks (strong
-scaling, the long-context configuration).
+Every run (N = 1 included) also measures the long-context configuration the way the baseline
+names it: C4's 32 heads of one N=16384 sequence split into N contiguous blocks of 32/N heads
+(fused_attn.sharding), every rank regenerating the seed-3 tensor and taking its block (strong
+scaling, ``secondary.c4_strong``).  After its timing, each rank's LSE and per-head O checksums are
+all-gathered and rank 0 compares them with one launch over all 32 heads on its own GPU (the same
+kernel on the same inputs: bit-identical).  ``--workload C4`` makes that split the headline.
 
 ``--impl reference``: the reference's CPU implementation of the path (its fp64 oracle, which is
 the only implementation of the path that runs on this machine class besides ours) on the host
-cores, on the same workload/metric, each step a bounded sample (one (b, h) head).
+cores, on the same workload/metric, each step a bounded sample (one (b, h) head).  It loads the
+workload generator by file path and the reference's compiled oracle, nothing of the fused_attn
+package, and reports the same ``config`` as our line.
 """
 
 from __future__ import annotations
@@ -48,6 +54,7 @@ from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "fused-attention-cuda_b200"))
+WORKLOADS_PY = ROOT / "fused-attention-cuda_b200" / "fused_attn" / "workloads.py"
 
 METRIC = "SDPA fwd ms & TFLOP/s, B2H8N2048 D64/128 fp16, % of B200 tensor peak"
 UNIT = "TFLOP/s"
@@ -202,13 +209,59 @@ class ClockSampler:
 
 
 # ------------------------------------------------------------------------------------------
-def workload_config(name: str):
-    from fused_attn.workloads import CONFIGS
+_WL = None
 
+
+def workloads():
+    """fused_attn/workloads.py (seeded generator, FLOP/byte models, CONFIGS) loaded by file path,
+    so that the reference arm does not import the fused_attn package (whose __init__ maps the
+    CUDA extension)."""
+    global _WL
+    if _WL is None:
+        import importlib.util
+
+        spec = importlib.util.spec_from_file_location("fa_bench_workloads", WORKLOADS_PY)
+        mod = importlib.util.module_from_spec(spec)
+        sys.modules["fa_bench_workloads"] = mod  # dataclasses resolve their module by name
+        spec.loader.exec_module(mod)
+        _WL = mod
+    return _WL
+
+
+def workload_config(name: str):
     key = {"c2": "C2", "c2c": "C2c", "c3": "C3", "c3bf16": "C3bf16", "c4": "C4"}.get(name.lower())
     if key is None:
         raise SystemExit(f"unknown workload {name}")
-    return CONFIGS[key]
+    return workloads().CONFIGS[key]
+
+
+def headline_config(base, world: int) -> tuple[dict, object, str]:
+    """The JSON line's ``config`` for workload `base` on `world` ranks (both arms print the same),
+    the per-rank configuration, and the scaling kind."""
+    wl = workloads()
+    if base.name == "C4":
+        hs = base.H // world
+        cfg = wl.Config("C4", base.B, hs, base.N, base.D, base.dtype, base.seed, base.causal)
+        scaling, global_batch = "strong", base.B
+        parallelism = f"head-sharded x{world} ({hs} heads/GPU), no collective"
+        l2 = "flushed before every timed launch (256 MiB write); inputs > L2"
+    else:
+        cfg = base
+        scaling, global_batch = "weak", base.B * world
+        parallelism = f"batch-sharded dp{world}, no collective"
+        l2 = "flushed before every timed launch (256 MiB write); inputs < L2"
+    config = {
+        "workload": base.label(),
+        "global_batch": global_batch,
+        "seq_len": cfg.N,
+        "heads_per_gpu": cfg.H,
+        "head_dim": cfg.D,
+        "causal": cfg.causal,
+        "parallelism": parallelism,
+        "l2": l2,
+        "timing": "CUDA events per launch on the launching stream; max over ranks",
+    }
+    return config, cfg, scaling
 
 
 def time_kernel(fn, steps: int, warmup: int, flush, stream) -> list[float]:
@@ -233,8 +286,8 @@ def time_kernel(fn, steps: int, warmup: int, flush, stream) -> list[float]:
 def cpu_sample(cfg, budget_s: float, threads: int) -> dict:
     """Times the reference's fp64 oracle on whole (b, h) heads of `cfg` until `budget_s`."""
     import oracle
-    from fused_attn.workloads import attention_flops, make_qkv
 
+    attention_flops, make_qkv = workloads().attention_flops, workloads().make_qkv
     kind = "reference" if oracle.ref_available() else "port"
     heads_done, flops, elapsed = 0, 0.0, 0.0
     total_heads = cfg.B * cfg.H
@@ -265,9 +318,12 @@ def run_reference(args) -> int:
         return 0
     sys.path.insert(0, str(ROOT))
     import oracle
-    from fused_attn.workloads import attention_flops, make_qkv
 
-    cfg = workload_config(args.workload)
+    wl = workloads()
+    attention_flops, make_qkv = wl.attention_flops, wl.make_qkv
+    base = workload_config(args.workload)
+    config, _, scaling = headline_config(base, max(1, args.gpus))
+    cfg = base
     threads = oracle.default_threads()
     kind = "reference" if oracle.ref_available() else "port"
     q, k, v = make_qkv(cfg.B, cfg.H, cfg.N, cfg.D, dtype=cfg.dtype, hkv=cfg.hkv, seed=cfg.seed)
@@ -295,11 +351,11 @@ def run_reference(args) -> int:
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * sum(times) / len(times), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "fp64",
+        "scaling": scaling, "vs_baseline": None, "dtype": "fp64",
         "data": f"synthetic: torch.randn seed {cfg.seed}, rounded to {dt}, upcast to fp64",
-        "config": {"workload": cfg.label(), "global_batch": cfg.B, "seq_len": cfg.N,
-                   "heads": cfg.H, "head_dim": cfg.D, "causal": cfg.causal,
-                   "step": "one (b, h) head of the workload (bounded sample)"},
+        "config": config,
+        "protocol": "host wall clock (perf_counter) per step; one (b, h) head of the workload per "
+                    "step (bounded sample), the reference's fp64 oracle on all host threads",
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
                          "sample": "one (b, h) head per step, cycling through the heads"},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -313,7 +369,9 @@ def run_ours(args) -> int:
     import torch.distributed as dist
 
     import fused_attn
-    from fused_attn.workloads import Config, attention_bytes, attention_flops, make_qkv
+
+    wl = workloads()
+    attention_bytes, attention_flops, make_qkv = wl.attention_bytes, wl.attention_flops, wl.make_qkv
 
     world = env_int("WORLD_SIZE", 1)
     rank = env_int("RANK", 0)
@@ -330,27 +388,22 @@ def run_ours(args) -> int:
     if not fused_attn.is_available():
         raise SystemExit("fused_attn._C is not built (python fused-attention-cuda_b200/build.py)")
 
+    from fused_attn import sharding
+
     base = workload_config(args.workload)
+    if base.name == "C4" and base.H % world:
+        raise SystemExit(f"C4 has {base.H} heads, not divisible by {world}")
+    config, cfg, scaling = headline_config(base, world)
     if base.name == "C4":
         # Strong scaling: the 32 heads of one sequence split into contiguous per-rank blocks.
-        if base.H % world:
-            raise SystemExit(f"C4 has {base.H} heads, not divisible by {world}")
-        hs = base.H // world
         q_all, k_all, v_all = make_qkv(base.B, base.H, base.N, base.D, dtype=base.dtype,
                                        seed=base.seed)
-        sl = slice(rank * hs, (rank + 1) * hs)
-        q, k, v = (t[:, sl].contiguous().to(dev) for t in (q_all, k_all, v_all))
+        q, k, v = (t.to(dev) for t in sharding.shard_heads(q_all, k_all, v_all, world, rank))
         del q_all, k_all, v_all
-        cfg = Config("C4", base.B, hs, base.N, base.D, base.dtype, base.seed, base.causal)
-        scaling, global_batch = "strong", base.B
-        parallelism = f"head-sharded x{world} ({hs} heads/GPU), no collective"
     else:
         # Weak scaling: same per-GPU workload, rank r owns batch shard r (seed + r).
-        cfg = base
-        q, k, v = make_qkv(cfg.B, cfg.H, cfg.N, cfg.D, dtype=cfg.dtype, seed=cfg.seed + rank,
-                           device=dev)
-        scaling, global_batch = "weak", cfg.B * world
-        parallelism = f"batch-sharded dp{world}, no collective"
+        q, k, v = make_qkv(cfg.B, cfg.H, cfg.N, cfg.D, dtype=cfg.dtype,
+                           seed=sharding.batch_seed(cfg.seed, rank), device=dev)
 
     stream = torch.cuda.current_stream(dev)
     flush = torch.empty(FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
@@ -446,6 +499,8 @@ def run_ours(args) -> int:
 
     secondary = None
     cpu_base = None
+    c4 = c4_strong(world, rank, dev, stream, flush, max(5, min(args.steps, 20)), args.warmup) \
+        if not args.quick and base.name != "C4" else None
     if rank == 0 and world == 1 and not args.quick:
         secondary = secondary_measurements(cfg, q, k, v, flush, stream, max(20, min(args.steps, 200)))
         cpu_base = cpu_sample(cfg, args.cpu_budget, threads=_host_threads())
@@ -471,17 +526,7 @@ def run_ours(args) -> int:
         "vs_baseline": None,
         "dtype": dt,
         "data": f"synthetic: torch.randn iid N(0,1), seed {cfg.seed}(+rank), [B,H,N,D] contiguous",
-        "config": {
-            "workload": cfg.label() if base.name != "C4" else base.label(),
-            "global_batch": global_batch,
-            "seq_len": cfg.N,
-            "heads_per_gpu": cfg.H,
-            "head_dim": cfg.D,
-            "causal": cfg.causal,
-            "parallelism": parallelism,
-            "l2": "flushed before every timed launch (256 MiB write); inputs < L2",
-            "timing": "CUDA events per launch on the launching stream; max over ranks",
-        },
+        "config": config,
         "roofline": {
             "bound": "tensor",
             "achieved": achieved,
@@ -508,10 +553,64 @@ def run_ours(args) -> int:
         "clocks": clocks,
         "kernel_ms": {"median": statistics.median(times), "p10": _pct(times, 10),
                       "p90": _pct(times, 90), "min": min(times)},
-        "secondary": secondary,
+        "secondary": dict(secondary or {}, **({"c4_strong": c4} if c4 else {})) or None,
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+def c4_strong(world: int, rank: int, dev, stream, flush, steps: int, warmup: int) -> dict:
+    """secondary.c4_strong: C4 (B1 H32 N16384 D128 bf16 causal, seed 3) split by heads over the
+    ranks (fused_attn.sharding: 32/world contiguous heads each, no collective on the data path),
+    max-over-ranks device time; then O and LSE of every rank are all-gathered (off the hot path)
+    and rank 0 compares them with one launch over all 32 heads on its own GPU, which it also
+    times (strong-scaling efficiency = one-GPU time / (world x sharded time))."""
+    import torch
+    import torch.distributed as dist
+
+    from fused_attn import sharding
+
+    wl = workloads()
+    base = wl.CONFIGS["C4"]
+    if base.H % world:
+        return {"skipped": f"{base.H} heads do not split evenly over {world} ranks"}
+    q_all, k_all, v_all = wl.make_qkv(base.B, base.H, base.N, base.D, dtype=base.dtype,
+                                      seed=base.seed)
+    h0, h1 = sharding.head_range(base.H, world, rank)
+    q, k, v = (t.to(dev) for t in sharding.shard_heads(q_all, k_all, v_all, world, rank))
+    scale = 1.0 / math.sqrt(base.D)
+    op = torch.ops.fused_attn.forward
+    if world > 1:
+        dist.barrier()
+    times = time_kernel(lambda: op(q, k, v, True, scale), steps, max(3, min(warmup, 5)), flush,
+                        stream)
+    t = torch.tensor([sum(times)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t[0]) / steps
+    o, lse = op(q, k, v, True, scale)
+    torch.cuda.synchronize()
+    if world > 1:
+        o, lse = sharding.gather_heads(o, world), sharding.gather_heads(lse, world)
+    flops = wl.attention_flops(base.B, base.H, base.N, base.D, True)
+    out = {"workload": base.label(), "heads_per_gpu": h1 - h0, "ranks": world,
+           "ms_max_over_ranks": ms, "tflops": flops / ms / 1e9,
+           "protocol": f"{steps} launches per rank, CUDA events on the launching stream, L2 "
+                       "flushed before each (inputs > L2 anyway); max over ranks"}
+    if rank == 0:
+        qf, kf, vf = (t.to(dev) for t in (q_all, k_all, v_all))
+        t1 = time_kernel(lambda: op(qf, kf, vf, True, scale), steps, 3, flush, stream)
+        of, lf = op(qf, kf, vf, True, scale)
+        torch.cuda.synchronize()
+        ms1 = sum(t1) / steps
+        out.update({"one_gpu_ms": ms1, "one_gpu_tflops": flops / ms1 / 1e9,
+                    "efficiency_vs_one_gpu": ms1 / (world * ms),
+                    "o_bitwise_equal_to_one_launch": bool(torch.equal(o, of)),
+                    "lse_bitwise_equal_to_one_launch": bool(torch.equal(lse, lf))})
+        del qf, kf, vf, of, lf
+    del q, k, v, o, lse
+    torch.cuda.empty_cache()
+    return out
 
 
 def _host_threads() -> int:
@@ -533,7 +632,8 @@ def secondary_measurements(cfg, q, k, v, flush, stream, steps):
     import torch
     import torch.nn.functional as F
 
-    from fused_attn.workloads import CONFIGS, attention_flops, make_qkv
+    wl = workloads()
+    CONFIGS, attention_flops, make_qkv = wl.CONFIGS, wl.attention_flops, wl.make_qkv
 
     out = {}
     fl = attention_flops(cfg.B, cfg.H, cfg.N, cfg.D, cfg.causal)
@@ -547,6 +647,15 @@ def secondary_measurements(cfg, q, k, v, flush, stream, steps):
                     flush, stream)
     ms = statistics.median(t)
     out["ours_median"] = {"ms_median": ms, "tflops": fl / ms / 1e9}
+    # Every SDPA backend that accepts each BASELINE shape, same protocol (the reference's bench
+    # times EFFICIENT, FLASH, cuDNN: bench/bench.py:279-356); ours against the best of them.
+    for name in ("C3", "C3bf16", "C2", "C2c"):
+        c = CONFIGS[name]
+        if name == cfg.name:
+            q2, k2, v2 = q, k, v
+        else:
+            q2, k2, v2 = make_qkv(c.B, c.H, c.N, c.D, dtype=c.dtype, seed=c.seed, device=q.device)
+        out[f"sdpa_backends_{name}"] = sdpa_backends(c, q2, k2, v2, flush, stream, steps)
     # CUDA-graph batch of 20 launches (no flush in between: warm L2), labelled as such.
     g = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream()
@@ -598,6 +707,41 @@ def secondary_measurements(cfg, q, k, v, flush, stream, steps):
                      "sdpa_fp32_tflops": f3 / statistics.median(ts) / 1e9}
     out["C5_gpt2_block"] = gpt_block_measurements(q.device)
     return out
+
+
+def sdpa_backends(c, q, k, v, flush, stream, steps) -> dict:
+    """TFLOP/s of our op and of each PyTorch SDPA backend (FLASH, cuDNN, EFFICIENT) that accepts
+    the shape, on the same inputs and protocol; `best_sdpa` and our ratio to it."""
+    import torch
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+
+    fl = workloads().attention_flops(c.B, c.H, c.N, c.D, c.causal)
+    scale = 1.0 / math.sqrt(c.D)
+    res = {"workload": c.label()}
+    t = time_kernel(lambda: torch.ops.fused_attn.forward(q, k, v, c.causal, scale), steps, 10,
+                    flush, stream)
+    res["ours_tflops"] = fl / statistics.median(t) / 1e9
+    best = None
+    for name, be in (("flash", SDPBackend.FLASH_ATTENTION), ("cudnn", SDPBackend.CUDNN_ATTENTION),
+                     ("efficient", SDPBackend.EFFICIENT_ATTENTION)):
+        try:
+            with sdpa_kernel([be]):
+                F.scaled_dot_product_attention(q, k, v, is_causal=c.causal)
+                t = time_kernel(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=c.causal),
+                                steps, 10, flush, stream)
+        except RuntimeError as e:
+            res[f"sdpa_{name}"] = {"refused": str(e).splitlines()[0][:120]}
+            continue
+        tf = fl / statistics.median(t) / 1e9
+        res[f"sdpa_{name}_tflops"] = tf
+        if best is None or tf > best[1]:
+            best = (name, tf)
+    if best is not None:
+        res["best_sdpa"] = best[0]
+        res["best_sdpa_tflops"] = best[1]
+        res["ours_over_best_sdpa"] = res["ours_tflops"] / best[1]
+    return res
 
 
 def gpt_block_measurements(device, warmup: int = 10, iters: int = 50) -> dict:
