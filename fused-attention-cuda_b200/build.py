@@ -8,6 +8,11 @@ Products (git-ignored, but they travel to the GPU box with the repository snapsh
   so the library loads with or without torch in the process.
 * ``fused_attn/_C<EXT_SUFFIX>`` -- the PyTorch operator library (csrc/ext.cpp), host C++ only,
   linked against libfa_sm100.so through an ``$ORIGIN`` rpath.
+* ``fused_attn/libfa_sm100_checks.so`` -- the same library built with ``-DFA_DEBUG_CHECKS``: device
+  index/address checks that record a status bit (fa_last_device_error -> cudaErrorAssert) and skip
+  the access instead of trapping; the tests run it against the release build.
+* ``fused_attn/fa_bench`` -- the torch-free benchmark (csrc/fa_bench.cpp): links libfa_sm100.so
+  through include/fa_sm100.h alone and self-checks against the CPU oracle before timing.
 
 nvcc cross-compiles without a GPU, so this runs on the CPU build host too.
 """
@@ -76,23 +81,54 @@ def _run(cmd: list[str], verbose: bool) -> None:
     subprocess.run(cmd, check=True)
 
 
-def build_kernels(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False) -> Path:
-    BUILD_DIR.mkdir(exist_ok=True)
+def checks_lib_path() -> Path:
+    return OUT_DIR / "libfa_sm100_checks.so"
+
+
+def build_kernels(force: bool = False, verbose: bool = False, ptxas_verbose: bool = False,
+                  checks: bool = False) -> Path:
+    """libfa_sm100.so, or with `checks` libfa_sm100_checks.so (-DFA_DEBUG_CHECKS)."""
+    obj_dir = BUILD_DIR / ("checks" if checks else "")
+    obj_dir.mkdir(parents=True, exist_ok=True)
     headers = [CSRC / h for h in KERNEL_HEADERS] + [INCLUDE / "fa_sm100.h"]
-    objs = []
+    defs = ["-DFA_DEBUG_CHECKS"] if checks else []
+    jobs, objs = [], []
     for src in KERNEL_SOURCES:
         s = CSRC / src
-        o = BUILD_DIR / (s.stem + ".o")
+        o = obj_dir / (s.stem + ".o")
         if force or _stale(o, [s, *headers]):
             extra = ["-Xptxas", "-v"] if ptxas_verbose else []
-            _run([NVCC, "-ccbin", host_cxx(), *NVCC_FLAGS, *extra, "-c", str(s), "-o", str(o)],
-                 verbose)
+            jobs.append([NVCC, "-ccbin", host_cxx(), *NVCC_FLAGS, *defs, *extra, "-c", str(s), "-o",
+                         str(o)])
         objs.append(o)
-    lib = lib_path()
+    procs = []
+    for cmd in jobs:  # the translation units compile in parallel
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        procs.append((cmd, subprocess.Popen(cmd)))
+    for cmd, pr in procs:
+        if pr.wait() != 0:
+            raise subprocess.CalledProcessError(pr.returncode, cmd)
+    lib = checks_lib_path() if checks else lib_path()
     if force or _stale(lib, objs):
-        _run([NVCC, "-ccbin", host_cxx(), *ARCH_FLAGS, "-shared", "-Xlinker", f"-soname={LIB_NAME}", "-o", str(lib),
-              *map(str, objs)], verbose)
+        _run([NVCC, "-ccbin", host_cxx(), *ARCH_FLAGS, "-shared", "-Xlinker", f"-soname={lib.name}",
+              "-o", str(lib), *map(str, objs)], verbose)
     return lib
+
+
+def bench_path() -> Path:
+    return OUT_DIR / "fa_bench"
+
+
+def build_bench(force: bool = False, verbose: bool = False) -> Path:
+    """The torch-free C++ harness: host code only, the C ABI library and the CUDA runtime."""
+    src = CSRC / "fa_bench.cpp"
+    out = bench_path()
+    if force or _stale(out, [src, INCLUDE / "fa_sm100.h", lib_path()]):
+        _run([NVCC, "-ccbin", host_cxx(), *ARCH_FLAGS, "-O2", "-std=c++17", f"-I{INCLUDE}", str(src), "-o",
+              str(out), f"-L{OUT_DIR}", "-l:" + LIB_NAME, "-Xlinker", "-rpath,$ORIGIN", "-ldl"],
+             verbose)
+    return out
 
 
 def build_ext(force: bool = False, verbose: bool = False) -> Path:
@@ -120,6 +156,8 @@ def build_ext(force: bool = False, verbose: bool = False) -> Path:
 
 def build(force: bool = False, verbose: bool = False, ext: bool = True) -> None:
     build_kernels(force=force, verbose=verbose)
+    build_kernels(force=force, verbose=verbose, checks=True)
+    build_bench(force=force, verbose=verbose)
     if ext:
         build_ext(force=force, verbose=verbose)
 
@@ -133,6 +171,8 @@ def main(argv: list[str] | None = None) -> int:
     args = ap.parse_args(argv)
     build_kernels(force=args.force or args.ptxas_verbose, verbose=args.verbose,
                   ptxas_verbose=args.ptxas_verbose)
+    build_kernels(force=args.force, verbose=args.verbose, checks=True)
+    build_bench(force=args.force, verbose=args.verbose)
     if not args.no_ext:
         build_ext(force=args.force, verbose=args.verbose)
     print(f"built {lib_path()}" + ("" if args.no_ext else f" and {ext_path()}"))
