@@ -566,6 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int i = item_index(rnd, G, cta);
       if (i >= args.n_items) break;
       const Item item = decode_item<CAUSAL>(i, args);
+      FA_DCHECK(item.bh < args.n_bh && item.q_tile >= 0 && item.q_tile < args.n_q_tiles);
       const int q0 = item.q_tile * kBlockM;
       const int row = q0 + r;
       const int kv_end = CAUSAL ? min(args.N, q0 + kBlockM) : args.N;
@@ -582,7 +583,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         FA_TRACE_EV(rnd == 0 && r == 0, 2, g, t);
         float s[BG];
-        load_s_row<BG>(tl + s_col, s);
+        if (FA_DCHECK(s_col + BG <= L::kTmemCols)) load_s_row<BG>(tl + s_col, s);
         // S is in registers: the tensor core may compute the next round into it.
         tc_fence_before();
         mbar_arrive(bar(L::kBarSFree));
@@ -634,7 +635,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (!ok) break;
           ++pvc;
           tc_fence_after();
-          if (__any_sync(0xffffffffu, resc)) {
+          if (__any_sync(0xffffffffu, resc) && FA_DCHECK(o_col + D <= L::kTmemCols)) {
             // 64 columns per wait: two loads in flight, then both scaled and stored back.
 #pragma unroll
             for (int c = 0; c < D; c += 64) {
@@ -653,7 +654,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             }
           }
         }
-        if (!(kBf16 && comp)) {
+        if (!(kBf16 && comp) && FA_DCHECK(p_col + BG / 2 <= L::kTmemCols)) {
           tmem_st16(tl + p_col, &pk[0]);
           tmem_st16(tl + p_col + 16, &pk[16]);
         }
@@ -682,7 +683,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const float inv_l = (l > 0.f) ? 1.f / l : 0.f;
       const float f0 = a0 * inv_l, f1 = a1 * inv_l;
       const bool in_range = row < args.N;
-      if (g == 0 && in_range) {
+      if (g == 0 && in_range && FA_DCHECK(item.bh < args.n_bh)) {
         args.lse[static_cast<size_t>(item.bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)] =
             (l > 0.f && m != -INFINITY) ? fmaf(m, args.scale, logf(l)) : INFINITY;
       }
@@ -718,6 +719,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int k2 = 0; k2 < 16; ++k2) pk[k2] = pack2<T>(o[2 * k2], o[2 * k2 + 1]);
         uint8_t* rowp = smem + L::kOStOff + (c / 64) * L::kQChunkBytes + r * 128;
+        if (!FA_DCHECK((c / 64) * L::kQChunkBytes + r * 128 + 128 <= L::kOStBytes)) continue;
 #pragma unroll
         for (int k2 = 0; k2 < 4; ++k2) {
           const int unit = (c % 64) / 8 + k2;

@@ -449,6 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int i = item_index(rnd, G, cta);
       if (i >= args.n_items) break;
       const Item item = decode_item<CAUSAL>(i, args);
+      FA_DCHECK(item.bh < args.n_bh && item.q_tile >= 0 && item.q_tile < args.n_q_tiles);
       const int q0 = item.q_tile * kBlockM;
       const int row = q0 + r;
       const int kv_end = CAUSAL ? min(args.N, q0 + kBlockM) : args.N;
@@ -468,7 +469,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tc_fence_after();
         FA_TRACE_EV(rnd == 0 && r == 0, 2, g, t);
         float s[BN];
-        load_s_row<BN>(tl + s_col, s);
+        if (FA_DCHECK(s_col + BN <= L::kTmemCols)) load_s_row<BN>(tl + s_col, s);
         FA_TRACE_EV(rnd == 0 && r == 0, 4, g, t);
         const int kv0 = j * BN;
         if ((CAUSAL && kv0 + BN - 1 > q0) || kv0 + BN > args.N) {
@@ -501,7 +502,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         m_ref = m_use;
         // O_g correction.  S_g(t) completing implies PV_g(t-1) completed (the commit of S_g(t)
         // covers every MMA issued before it), and PV_g(t) waits for our arrival below.
-        if (t > 0 && __any_sync(0xffffffffu, resc)) {
+        if (t > 0 && __any_sync(0xffffffffu, resc) && FA_DCHECK(o_col + D <= L::kTmemCols)) {
 #pragma unroll
           for (int c = 0; c < D; c += 32) {
             uint32_t u[32];
@@ -565,7 +566,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k2 = 0; k2 < 32; ++k2) o[k2] = fmaf(__uint_as_float(u1[k2]), f1, o[k2]);
         }
         if constexpr (kTf32) {
-          if (in_range) {
+          if (in_range && FA_DCHECK(item.bh < args.n_bh && c + 32 <= D)) {
             float4* dst = reinterpret_cast<float4*>(orow + c);
 #pragma unroll
             for (int k2 = 0; k2 < 8; ++k2) {
@@ -577,6 +578,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
           for (int k2 = 0; k2 < 16; ++k2) pk[k2] = pack2<T>(o[2 * k2], o[2 * k2 + 1]);
           uint8_t* rowp = smem + L::kOStOff + (c / 64) * L::kQChunkBytes + r * 128;
+          if (!FA_DCHECK((c / 64) * L::kQChunkBytes + r * 128 + 128 <= L::kOStBytes)) continue;
 #pragma unroll
           for (int k2 = 0; k2 < 4; ++k2) {
             const int unit = (c % 64) / 8 + k2;
@@ -588,7 +590,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // O_0 and O_1 have been read: the next item's first PVs may overwrite them.
       tc_fence_before();
       mbar_arrive(bar(L::kBarOFree));
-      if (g == 0 && in_range) {
+      if (g == 0 && in_range && FA_DCHECK(item.bh < args.n_bh)) {
         args.lse[static_cast<size_t>(item.bh) * static_cast<size_t>(args.N) + static_cast<size_t>(row)] =
             (l > 0.f && m != -INFINITY) ? fmaf(m, args.scale, logf(l)) : INFINITY;
       }
@@ -1003,7 +1005,8 @@ cudaError_t read_and_clear_status(unsigned int* bits) {
   }
   if (bits != nullptr) *bits = v;
   if (e != cudaSuccess) return e;
-  return v != 0 ? cudaErrorLaunchTimeout : cudaSuccess;
+  if (v == 0) return cudaSuccess;
+  return (v & kStBounds) != 0 ? cudaErrorAssert : cudaErrorLaunchTimeout;
 }
 
 }  // namespace fa_sm100

@@ -32,6 +32,19 @@ __device__ long long g_trace_t0[kTraceCtas];
   } while (0)
 #endif
 
+// FA_DEBUG_CHECKS builds (-DFA_DEBUG_CHECKS; build.py makes libfa_sm100_checks.so): index and
+// address checks in front of the kernels' computed accesses -- tensor-memory columns against the
+// allocation, shared-memory offsets against the layout, global LSE / O / workspace indices
+// against the tensor sizes, work items against the item count.  A failed check sets kStBounds in
+// g_status (fa_last_device_error then returns cudaErrorAssert) and the guarded access is skipped:
+// nothing traps, the kernel runs on, and its bounded waits end any hand-off the skip disturbs.
+// Release builds compile every check to `true`.
+#ifdef FA_DEBUG_CHECKS
+#define FA_DCHECK(cond) ((cond) ? true : (atomicOr(&g_status, kStBounds), false))
+#else
+#define FA_DCHECK(cond) true
+#endif
+
 namespace {
 
 constexpr int kBlockM = 128;

@@ -60,6 +60,7 @@ enum StatusBits : unsigned int {
   kStDrain = 1u << 7,    // exit path waiting for in-flight copies / MMAs
   kStSFree = 1u << 8,    // MMA warp waiting for the softmax warps to read S (lookahead kernel)
   kStPFree = 1u << 9,    // softmax warps waiting for a PV to release P (lookahead kernel)
+  kStBounds = 1u << 10,  // FA_DEBUG_CHECKS builds: an index or address check failed
 };
 
 }  // namespace fa_sm100

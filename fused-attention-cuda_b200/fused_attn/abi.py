@@ -12,6 +12,7 @@ import ctypes
 from pathlib import Path
 
 LIB_PATH = Path(__file__).resolve().parent / "libfa_sm100.so"
+CHECKS_LIB_PATH = Path(__file__).resolve().parent / "libfa_sm100_checks.so"
 
 # Every function declared in include/fa_sm100.h (the CPU test checks the header and this list
 # against the library's exported symbols).
@@ -78,42 +79,55 @@ def lib() -> ctypes.CDLL:
             raise ImportError(
                 f"{LIB_PATH} is not built; run `python fused-attention-cuda_b200/build.py`"
             )
-        L = ctypes.CDLL(str(LIB_PATH))
-        vp, i, u = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint
-        L.fa_forward.argtypes = [i, i, vp, vp, vp, vp, vp, vp, ctypes.POINTER(FaParams), vp]
-        L.fa_forward.restype = i
-        L.fa_forward_strided.argtypes = [i, i, vp, vp, vp, vp, vp, vp, ctypes.POINTER(FaParams),
-                                         ctypes.POINTER(FaStrides), vp]
-        L.fa_forward_strided.restype = i
-        L.fa_combine.argtypes = [i, i, ctypes.POINTER(vp), ctypes.POINTER(vp), vp, vp, i, i, i, i,
-                                 vp]
-        L.fa_combine.restype = i
-        L.fa_forward_noalloc.argtypes = [i, i, vp, vp, vp, vp, vp, ctypes.POINTER(FaParams), vp]
-        L.fa_forward_noalloc.restype = i
-        L.fa_noalloc_scratch_bytes.argtypes = []
-        L.fa_noalloc_scratch_bytes.restype = ctypes.c_size_t
-        L.fa_workspace_bytes.argtypes = [i, i, ctypes.POINTER(FaParams)]
-        L.fa_workspace_bytes.restype = ctypes.c_size_t
-        L.fa_impl_supports.argtypes = [i, i, i, i]
-        L.fa_impl_supports.restype = i
-        L.fa_set_debug_overrides.argtypes = [i, i]
-        L.fa_set_debug_overrides.restype = None
-        L.fa_get_debug_overrides.argtypes = [i, ctypes.POINTER(i), ctypes.POINTER(i)]
-        L.fa_get_debug_overrides.restype = None
-        L.fa_impl_name.argtypes = [i]
-        L.fa_impl_name.restype = ctypes.c_char_p
-        L.fa_dtype_name.argtypes = [i]
-        L.fa_dtype_name.restype = ctypes.c_char_p
-        L.fa_dtype_size.argtypes = [i]
-        L.fa_dtype_size.restype = ctypes.c_size_t
-        L.fa_last_device_error.argtypes = [ctypes.POINTER(u)]
-        L.fa_last_device_error.restype = i
-        L.fa_set_wait_timeout_ns.argtypes = [ctypes.c_ulonglong]
-        L.fa_set_wait_timeout_ns.restype = None
-        L.fa_debug_set_skip_kv_tile.argtypes = [i]
-        L.fa_debug_set_skip_kv_tile.restype = None
-        _lib = L
+        _lib = configure(ctypes.CDLL(str(LIB_PATH)))
     return _lib
+
+
+def configure(L: ctypes.CDLL) -> ctypes.CDLL:
+    """Sets the argument and result types of every exported function on a loaded library (the
+    release libfa_sm100.so or its FA_DEBUG_CHECKS build)."""
+    vp, i, u = ctypes.c_void_p, ctypes.c_int, ctypes.c_uint
+    L.fa_forward.argtypes = [i, i, vp, vp, vp, vp, vp, vp, ctypes.POINTER(FaParams), vp]
+    L.fa_forward.restype = i
+    L.fa_forward_strided.argtypes = [i, i, vp, vp, vp, vp, vp, vp, ctypes.POINTER(FaParams),
+                                     ctypes.POINTER(FaStrides), vp]
+    L.fa_forward_strided.restype = i
+    L.fa_combine.argtypes = [i, i, ctypes.POINTER(vp), ctypes.POINTER(vp), vp, vp, i, i, i, i,
+                             vp]
+    L.fa_combine.restype = i
+    L.fa_forward_noalloc.argtypes = [i, i, vp, vp, vp, vp, vp, ctypes.POINTER(FaParams), vp]
+    L.fa_forward_noalloc.restype = i
+    L.fa_noalloc_scratch_bytes.argtypes = []
+    L.fa_noalloc_scratch_bytes.restype = ctypes.c_size_t
+    L.fa_workspace_bytes.argtypes = [i, i, ctypes.POINTER(FaParams)]
+    L.fa_workspace_bytes.restype = ctypes.c_size_t
+    L.fa_impl_supports.argtypes = [i, i, i, i]
+    L.fa_impl_supports.restype = i
+    L.fa_set_debug_overrides.argtypes = [i, i]
+    L.fa_set_debug_overrides.restype = None
+    L.fa_get_debug_overrides.argtypes = [i, ctypes.POINTER(i), ctypes.POINTER(i)]
+    L.fa_get_debug_overrides.restype = None
+    L.fa_impl_name.argtypes = [i]
+    L.fa_impl_name.restype = ctypes.c_char_p
+    L.fa_dtype_name.argtypes = [i]
+    L.fa_dtype_name.restype = ctypes.c_char_p
+    L.fa_dtype_size.argtypes = [i]
+    L.fa_dtype_size.restype = ctypes.c_size_t
+    L.fa_last_device_error.argtypes = [ctypes.POINTER(u)]
+    L.fa_last_device_error.restype = i
+    L.fa_set_wait_timeout_ns.argtypes = [ctypes.c_ulonglong]
+    L.fa_set_wait_timeout_ns.restype = None
+    L.fa_debug_set_skip_kv_tile.argtypes = [i]
+    L.fa_debug_set_skip_kv_tile.restype = None
+    return L
+
+
+def load_checks() -> ctypes.CDLL:
+    """The FA_DEBUG_CHECKS build (libfa_sm100_checks.so: device index checks that report
+    cudaErrorAssert instead of trapping), a separate library instance with its own state."""
+    if not CHECKS_LIB_PATH.exists():
+        raise ImportError(f"{CHECKS_LIB_PATH} is not built")
+    return configure(ctypes.CDLL(str(CHECKS_LIB_PATH)))
 
 
 def params(B: int, H: int, Hkv: int, N: int, D: int, scale: float, causal: bool) -> FaParams:

@@ -140,7 +140,9 @@ size_t fa_dtype_size(int dtype);
  * in the sm_100a kernel is bounded; a wait that runs out records a cause bit in a device-side
  * status word, the kernel drains its own copies, frees its tensor memory and exits normally.
  * This call synchronises the current device, returns cudaErrorLaunchTimeout (702) if any
- * launch since the previous call timed out (else the device's sticky error, or cudaSuccess),
+ * launch since the previous call timed out (cudaErrorAssert (710) instead when a build made
+ * with -DFA_DEBUG_CHECKS found an index out of range; else the device's sticky error, or
+ * cudaSuccess),
  * stores the cause bits in *detail when detail != NULL, and clears the status word. */
 int fa_last_device_error(unsigned int* detail);
 

@@ -29,9 +29,9 @@ def declared_functions() -> set[str]:
     return set(re.findall(r"\b(fa_[a-z_0-9]+)\s*\(", text))
 
 
-def exported_functions() -> set[str]:
-    out = subprocess.run(["nm", "-D", "--defined-only", str(abi.LIB_PATH)], capture_output=True,
-                         text=True, check=True).stdout
+def exported_functions(path=None) -> set[str]:
+    out = subprocess.run(["nm", "-D", "--defined-only", str(path or abi.LIB_PATH)],
+                         capture_output=True, text=True, check=True).stdout
     return {line.split()[-1] for line in out.splitlines() if " T " in line}
 
 
@@ -44,6 +44,17 @@ def test_library_exports_every_declared_symbol():
     lib = abi.lib()
     for name in declared:
         assert hasattr(lib, name)
+
+
+def test_checks_build_exports_the_same_symbols():
+    """libfa_sm100_checks.so (-DFA_DEBUG_CHECKS) is the same C ABI with device index checks."""
+    if not abi.CHECKS_LIB_PATH.exists():
+        pytest.skip("libfa_sm100_checks.so not built")
+    declared = declared_functions()
+    exported = {s for s in exported_functions(abi.CHECKS_LIB_PATH) if s.startswith("fa_")}
+    assert declared <= exported
+    chk = abi.load_checks()
+    assert chk.fa_impl_name(5) == b"tuned" and chk.fa_dtype_size(1) == 2
 
 
 def test_names_and_sizes_match_reference():
