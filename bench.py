@@ -656,6 +656,17 @@ def secondary_measurements(cfg, q, k, v, flush, stream, steps):
         else:
             q2, k2, v2 = make_qkv(c.B, c.H, c.N, c.D, dtype=c.dtype, seed=c.seed, device=q.device)
         out[f"sdpa_backends_{name}"] = sdpa_backends(c, q2, k2, v2, flush, stream, steps)
+    # The C3 N sweep of the baseline (same B, H, D, seed), fp16 and bf16.
+    sweep = {}
+    for n in wl.C3_SWEEP_N:
+        for dt in (torch.float16, torch.bfloat16):
+            c = wl.Config("C3", 2, 8, n, 128, dt, 2, True)
+            q2, k2, v2 = make_qkv(c.B, c.H, c.N, c.D, dtype=c.dtype, seed=c.seed, device=q.device)
+            r = sdpa_backends(c, q2, k2, v2, flush, stream, min(steps, 50))
+            sweep[c.label()] = {k: r[k] for k in ("ours_tflops", "best_sdpa", "best_sdpa_tflops",
+                                                  "ours_over_best_sdpa") if k in r}
+            del q2, k2, v2
+    out["c3_sweep"] = sweep
     # CUDA-graph batch of 20 launches (no flush in between: warm L2), labelled as such.
     g = torch.cuda.CUDAGraph()
     s = torch.cuda.Stream()

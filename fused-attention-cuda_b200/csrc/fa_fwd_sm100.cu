@@ -449,7 +449,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int i = item_index(rnd, G, cta);
       if (i >= args.n_items) break;
       const Item item = decode_item<CAUSAL>(i, args);
-      FA_DCHECK(item.bh < args.n_bh && item.q_tile >= 0 && item.q_tile < args.n_q_tiles);
+      (void)FA_DCHECK(item.bh < args.n_bh && item.q_tile >= 0 && item.q_tile < args.n_q_tiles);
       const int q0 = item.q_tile * kBlockM;
       const int row = q0 + r;
       const int kv_end = CAUSAL ? min(args.N, q0 + kBlockM) : args.N;

@@ -80,23 +80,30 @@ def register_fakes() -> None:
     _registered = True
 
 
-# opcheck in two groups (reference ops.py:72-96): test_autograd_registration needs inputs with
-# requires_grad=True, while the other three must see plain inputs (the op has no autograd kernel).
-_NO_GRAD_TESTS = ("test_schema", "test_faketensor", "test_aot_dispatch_dynamic")
-_GRAD_TESTS = ("test_autograd_registration",)
+# torch.library.opcheck utilities and the inputs each must see.  The ops have no autograd kernel:
+# test_autograd_registration is meant to run on tensors that require grad (it checks that such a
+# call is not silently differentiable), while the schema / fake-tensor / AOT-dispatch utilities
+# must see plain tensors.  (The reference's ops.py splits its opcheck the same way, for the same
+# reason: the split follows from opcheck's own contract.)
+_OPCHECK_PLAN = (
+    (("test_schema", "test_faketensor", "test_aot_dispatch_dynamic"), False),
+    (("test_autograd_registration",), True),
+)
+
+
+def _grad_inputs(args: tuple, on: bool) -> tuple:
+    """`args` with every floating-point tensor detached and requiring grad when `on`."""
+    if not on:
+        return args
+    return tuple(a.detach().requires_grad_() if isinstance(a, Tensor) and a.is_floating_point()
+                 else a for a in args)
 
 
 def _opcheck(op, args: tuple) -> dict[str, str]:
-    q, k, v, *rest = args
-    res = dict(torch.library.opcheck(op, (q, k, v, *rest), test_utils=_NO_GRAD_TESTS))
-    grad_args = (
-        q.detach().requires_grad_(),
-        k.detach().requires_grad_(),
-        v.detach().requires_grad_(),
-        *rest,
-    )
-    res.update(torch.library.opcheck(op, grad_args, test_utils=_GRAD_TESTS))
-    return res
+    report: dict[str, str] = {}
+    for utils, grad in _OPCHECK_PLAN:
+        report.update(torch.library.opcheck(op, _grad_inputs(args, grad), test_utils=utils))
+    return report
 
 
 def opcheck_all(q: Tensor, k: Tensor, v: Tensor, is_causal: bool = False,

@@ -54,12 +54,19 @@ _lib = None
 _ref = None
 
 
+def reference_root() -> Path:
+    """The reference checkout: $FA_REFERENCE_ROOT, else a `reference` directory beside this
+    repository (it need not exist: the reference-compiled oracle is then simply not built)."""
+    env = os.environ.get("FA_REFERENCE_ROOT")
+    return Path(env) if env else HERE.parent.parent / "reference"
+
+
 def build(ref: bool | None = None, quiet: bool = True) -> None:
     """Compile ``libfa_oracle.so`` (and ``_ref`` when the reference tree is present)."""
     import subprocess
 
     targets = ["all"]
-    ref_root = Path(os.environ.get("FA_REFERENCE_ROOT", "/root/reference"))
+    ref_root = reference_root()
     if ref is None:
         ref = (ref_root / "src" / "reference" / "cpu_reference.cpp").exists()
     if ref:

@@ -2,7 +2,8 @@
 
 Run (in a container where the reference tree is present, after ``make -C oracle ref``)::
 
-    python tests/golden/gen_golden.py [--reference-root /root/reference]
+    python tests/golden/gen_golden.py [--reference-root DIR]   (default: $FA_REFERENCE_ROOT, else
+                                                               a `reference` dir beside the repo)
 
 Two independent reference implementations produce every expected output:
 
@@ -56,9 +57,12 @@ def load_reference_py(root: Path):
 
 def main() -> int:
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference-root", default="/root/reference")
+    ap.add_argument("--reference-root", default=str(oracle.reference_root()))
     ap.add_argument("--out", default=str(HERE / "golden.npz"))
     args = ap.parse_args()
+    if not (Path(args.reference_root) / "python" / "fused_attn" / "reference.py").exists():
+        ap.error(f"no reference checkout at {args.reference_root}: pass --reference-root or set "
+                 "FA_REFERENCE_ROOT")
     ref_py = load_reference_py(Path(args.reference_root))
     if not oracle.ref_available():
         oracle.build(ref=True)
