@@ -30,9 +30,18 @@
 
 namespace {
 
-constexpr int64_t kMinStage = 1;
-constexpr int64_t kMaxStage = 5;
-constexpr int64_t kFirstLseStage = 3;
+// The reference's stage numbering (fa::Impl): 1..5, with an LSE from stage 3 up.  Constructing a
+// Stage is the range check.
+struct Stage {
+  static constexpr int kLowest = 1;
+  static constexpr int kHighest = 5;
+  static constexpr int kFirstWithLse = 3;
+  int value;
+  explicit Stage(int64_t s) : value(static_cast<int>(s)) {
+    TORCH_CHECK(s >= kLowest && s <= kHighest, "fused_attn: stage must be in 1..5, got ", s);
+  }
+  bool writes_lse() const { return value >= kFirstWithLse; }
+};
 
 int to_fa_dtype(at::ScalarType t) {
   if (t == at::kFloat) return FA_DTYPE_F32;
@@ -50,19 +59,17 @@ int dtype_from_name(const std::string& name) {
   return FA_DTYPE_BF16;
 }
 
-int current_sm() {
-  const cudaDeviceProp* prop = at::cuda::getCurrentDeviceProperties();
-  return prop->major * 10 + prop->minor;
+// fa_impl_supports' `sm` (major * 10 + minor) for a CUDA device index (-1: the current one).
+int sm_number(int device_index = -1) {
+  const cudaDeviceProp* prop = device_index < 0 ? at::cuda::getCurrentDeviceProperties()
+                                                : at::cuda::getDeviceProperties(device_index);
+  return 10 * prop->major + prop->minor;
 }
 
-void check_stage(int64_t stage) {
-  TORCH_CHECK(stage >= kMinStage && stage <= kMaxStage, "fused_attn: stage must be in 1..5, got ",
-              stage);
-}
-
-int checked_int(int64_t v, const char* what) {
-  TORCH_CHECK(v >= 0 && v <= std::numeric_limits<int>::max(), "fused_attn: ", what, "=", v,
-              " does not fit fa_params_t (int)");
+// A size or knob narrowed to the C ABI's `int` fields, rejected when it does not fit.
+int abi_int(int64_t v, const char* what) {
+  const bool fits = v >= 0 && v <= static_cast<int64_t>(std::numeric_limits<int>::max());
+  TORCH_CHECK(fits, "fused_attn: ", what, "=", v, " does not fit fa_params_t (int)");
   return static_cast<int>(v);
 }
 
@@ -117,42 +124,49 @@ fa_params_t make_params(const at::Tensor& q, const at::Tensor& k, const at::Tens
               scale);
 
   fa_params_t p;
-  p.B = checked_int(B, "B");
-  p.H = checked_int(H, "H");
-  p.Hkv = checked_int(Hkv, "Hkv");
-  p.N = checked_int(N, "N");
-  p.D = checked_int(D, "D");
+  p.B = abi_int(B, "B");
+  p.H = abi_int(H, "H");
+  p.Hkv = abi_int(Hkv, "Hkv");
+  p.N = abi_int(N, "N");
+  p.D = abi_int(D, "D");
   p.scale = static_cast<float>(scale);
   p.causal = is_causal ? 1 : 0;
   return p;
 }
 
+// The stage's outputs and scratch on q's device.  O takes q's layout (empty_like keeps the strides
+// of a dense view, e.g. the [B, H, N, D] transpose of a [B, N, H, D] buffer), so a head merge after
+// the op is a free view too.  The LSE is [B, H, N] fp32, or empty for a stage that writes none.
+struct StageBuffers {
+  at::Tensor o, lse, workspace;
+  StageBuffers(const at::Tensor& q, const fa_params_t& p, Stage stage, int dtype) {
+    const auto f32 = q.options().dtype(at::kFloat);
+    o = at::empty_like(q);
+    lse = stage.writes_lse() ? at::empty({p.B, p.H, p.N}, f32) : at::empty({0}, f32);
+    const std::size_t scratch = fa_workspace_bytes(stage.value, dtype, &p);
+    if (scratch > 0) {
+      workspace = at::empty({static_cast<int64_t>(scratch)}, q.options().dtype(at::kByte));
+    }
+  }
+  float* lse_ptr() { return lse.numel() > 0 ? lse.data_ptr<float>() : nullptr; }
+  void* workspace_ptr() { return workspace.defined() ? workspace.data_ptr() : nullptr; }
+};
+
 std::tuple<at::Tensor, at::Tensor> run_stage(const at::Tensor& q, const at::Tensor& k,
                                              const at::Tensor& v, bool is_causal, double scale,
-                                             int64_t stage, bool strided = false) {
-  check_stage(stage);
+                                             Stage stage, bool strided = false) {
   const fa_params_t p = make_params(q, k, v, is_causal, scale, strided);
   const c10::cuda::CUDAGuard guard(q.device());
-  const int impl = static_cast<int>(stage);
+  const int impl = stage.value;
   const int dtype = to_fa_dtype(q.scalar_type());
-  const int sm = current_sm();
-  TORCH_CHECK(fa_impl_supports(impl, dtype, p.D, sm), "fused_attn: stage ", stage, " (",
+  const int sm = sm_number(q.device().index());
+  TORCH_CHECK(fa_impl_supports(impl, dtype, p.D, sm), "fused_attn: stage ", impl, " (",
               fa_impl_name(impl), ") is not implemented for ", fa_dtype_name(dtype), " D=", p.D,
               " on sm_", sm);
-
-  // O takes q's layout (empty_like keeps the strides of a dense view, e.g. the [B, H, N, D]
-  // transpose of a [B, N, H, D] buffer), so a head merge after the op is a free view too.
-  at::Tensor o = at::empty_like(q);
-  const bool has_lse = stage >= kFirstLseStage;
-  at::Tensor lse = has_lse ? at::empty({p.B, p.H, p.N}, q.options().dtype(at::kFloat))
-                           : at::empty({0}, q.options().dtype(at::kFloat));
-  const std::size_t ws_bytes = fa_workspace_bytes(impl, dtype, &p);
-  at::Tensor workspace;
-  void* ws_ptr = nullptr;
-  if (ws_bytes > 0) {
-    workspace = at::empty({static_cast<int64_t>(ws_bytes)}, q.options().dtype(at::kByte));
-    ws_ptr = workspace.data_ptr();
-  }
+  StageBuffers out(q, p, stage, dtype);
+  at::Tensor& o = out.o;
+  const bool has_lse = stage.writes_lse();
+  void* ws_ptr = out.workspace_ptr();
   const cudaStream_t stream = at::cuda::getCurrentCUDAStream(q.device().index()).stream();
   int err;
   if (strided) {
@@ -164,56 +178,49 @@ std::tuple<at::Tensor, at::Tensor> run_stage(const at::Tensor& q, const at::Tens
       for (int d = 0; d < 3; ++d) dst[t][d] = static_cast<long long>(ts[t]->stride(d));
     }
     err = fa_forward_strided(impl, dtype, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
-                             has_lse ? lse.data_ptr<float>() : nullptr, ws_ptr, &p, &st, stream);
+                             has_lse ? out.lse_ptr() : nullptr, ws_ptr, &p, &st, stream);
   } else {
     err = fa_forward(impl, dtype, q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr(),
-                     has_lse ? lse.data_ptr<float>() : nullptr, ws_ptr, &p, stream);
+                     has_lse ? out.lse_ptr() : nullptr, ws_ptr, &p, stream);
   }
-  TORCH_CHECK(err == 0, "fused_attn: stage ", stage, " (", fa_impl_name(impl),
+  TORCH_CHECK(err == 0, "fused_attn: stage ", impl, " (", fa_impl_name(impl),
               ") failed: ", cudaGetErrorString(static_cast<cudaError_t>(err)));
-  return std::make_tuple(std::move(o), std::move(lse));
+  return std::make_tuple(std::move(out.o), std::move(out.lse));
 }
 
-// forward: the highest stage that fa_impl_supports() accepts (reference ext.cpp:174-188).
+// The stage `forward` runs: the highest one with an LSE that this device supports for the dtype
+// and head dim (the reference's forward picks its best stage the same way, ext.cpp:174-188).
+Stage best_stage(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, bool is_causal,
+                 double scale, bool strided) {
+  const fa_params_t p = make_params(q, k, v, is_causal, scale, strided);
+  const int dtype = to_fa_dtype(q.scalar_type());
+  const int sm = sm_number(q.device().index());
+  int chosen = 0;
+  for (int s = Stage::kHighest; s >= Stage::kFirstWithLse && chosen == 0; --s) {
+    if (fa_impl_supports(s, dtype, p.D, sm)) chosen = s;
+  }
+  TORCH_CHECK(chosen != 0, "fused_attn: no stage is implemented for ", fa_dtype_name(dtype),
+              " D=", p.D, " on sm_", sm);
+  return Stage(chosen);
+}
+
 std::tuple<at::Tensor, at::Tensor> forward_cuda(const at::Tensor& q, const at::Tensor& k,
                                                 const at::Tensor& v, bool is_causal,
                                                 double scale) {
-  const fa_params_t p = make_params(q, k, v, is_causal, scale);
-  const c10::cuda::CUDAGuard guard(q.device());
-  const int dtype = to_fa_dtype(q.scalar_type());
-  const int sm = current_sm();
-  for (int64_t stage = kMaxStage; stage >= kFirstLseStage; --stage) {
-    if (fa_impl_supports(static_cast<int>(stage), dtype, p.D, sm)) {
-      return run_stage(q, k, v, is_causal, scale, stage);
-    }
-  }
-  TORCH_CHECK(false, "fused_attn: no stage is implemented for ", fa_dtype_name(dtype), " D=", p.D,
-              " on sm_", sm);
-  return {};
+  return run_stage(q, k, v, is_causal, scale, best_stage(q, k, v, is_causal, scale, false));
 }
 
 // forward over strided [B, H, N, D] views (no counterpart in the reference): same stage choice.
 std::tuple<at::Tensor, at::Tensor> forward_strided_cuda(const at::Tensor& q, const at::Tensor& k,
                                                         const at::Tensor& v, bool is_causal,
                                                         double scale) {
-  const fa_params_t p = make_params(q, k, v, is_causal, scale, true);
-  const c10::cuda::CUDAGuard guard(q.device());
-  const int dtype = to_fa_dtype(q.scalar_type());
-  const int sm = current_sm();
-  for (int64_t stage = kMaxStage; stage >= kFirstLseStage; --stage) {
-    if (fa_impl_supports(static_cast<int>(stage), dtype, p.D, sm)) {
-      return run_stage(q, k, v, is_causal, scale, stage, true);
-    }
-  }
-  TORCH_CHECK(false, "fused_attn: no stage is implemented for ", fa_dtype_name(dtype), " D=", p.D,
-              " on sm_", sm);
-  return {};
+  return run_stage(q, k, v, is_causal, scale, best_stage(q, k, v, is_causal, scale, true), true);
 }
 
 std::tuple<at::Tensor, at::Tensor> forward_stage_cuda(const at::Tensor& q, const at::Tensor& k,
                                                       const at::Tensor& v, bool is_causal,
                                                       double scale, int64_t stage) {
-  return run_stage(q, k, v, is_causal, scale, stage);
+  return run_stage(q, k, v, is_causal, scale, Stage(stage));
 }
 
 // LSE-weighted merge of partials over disjoint key sets (no counterpart in the reference).
@@ -250,28 +257,24 @@ std::tuple<at::Tensor, at::Tensor> combine_cuda(at::TensorList o_parts, at::Tens
   const cudaStream_t stream = at::cuda::getCurrentCUDAStream(o0.device().index()).stream();
   const int err = fa_combine(to_fa_dtype(o0.scalar_type()), static_cast<int>(op.size()), op.data(),
                              lp.data(), out.data_ptr(), lse.data_ptr<float>(),
-                             checked_int(B, "B"), checked_int(H, "H"), checked_int(N, "N"),
-                             checked_int(D, "D"), stream);
+                             abi_int(B, "B"), abi_int(H, "H"), abi_int(N, "N"),
+                             abi_int(D, "D"), stream);
   TORCH_CHECK(err == 0, "fused_attn: combine failed: ",
               cudaGetErrorString(static_cast<cudaError_t>(err)));
   return std::make_tuple(std::move(out), std::move(lse));
 }
 
 void set_debug_overrides_op(int64_t block_m, int64_t block_n) {
-  fa_set_debug_overrides(checked_int(block_m, "block_m"), checked_int(block_n, "block_n"));
+  fa_set_debug_overrides(abi_int(block_m, "block_m"), abi_int(block_n, "block_n"));
 }
 
 bool impl_supports_op(int64_t stage, std::string dtype, int64_t D) {
-  check_stage(stage);
+  const Stage st(stage);
   if (c10::cuda::device_count() == 0) return false;
-  return fa_impl_supports(static_cast<int>(stage), dtype_from_name(dtype), checked_int(D, "D"),
-                          current_sm()) != 0;
+  return fa_impl_supports(st.value, dtype_from_name(dtype), abi_int(D, "D"), sm_number()) != 0;
 }
 
-std::string impl_name_op(int64_t stage) {
-  check_stage(stage);
-  return std::string(fa_impl_name(static_cast<int>(stage)));
-}
+std::string impl_name_op(int64_t stage) { return fa_impl_name(Stage(stage).value); }
 
 }  // namespace
 
@@ -296,17 +299,9 @@ TORCH_LIBRARY_IMPL(fused_attn, CUDA, m) {
   m.impl("forward_stage", &forward_stage_cuda);
 }
 
-extern "C" PyObject* PyInit__C(void) {
-  static struct PyModuleDef module_def = {
-      PyModuleDef_HEAD_INIT,
-      "_C",
-      "fused-attention B200 extension. The ops live in torch.ops.fused_attn.*",
-      -1,
-      nullptr,
-      nullptr,
-      nullptr,
-      nullptr,
-      nullptr,
-  };
-  return PyModule_Create(&module_def);
-}
+// A module with no functions of its own: importing it runs the TORCH_LIBRARY registrations above,
+// and the ops are reached as torch.ops.fused_attn.*.
+static PyModuleDef g_module = {PyModuleDef_HEAD_INIT, "_C",
+                               "B200 SDPA forward; ops under torch.ops.fused_attn", -1};
+
+extern "C" PyObject* PyInit__C(void) { return PyModule_Create(&g_module); }
