@@ -589,11 +589,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_arrive(bar(L::kBarSFree));
         const int kv0 = t * BR + g * BG;
         if ((CAUSAL && kv0 + BG - 1 > q0) || kv0 + BG > kv_end) {
+          // Key kv0 + c is visible to this row iff c <= lim (top-left causal, inside kv_end): one
+          // compare per score against a per-thread bound (measured +3-6 % on causal shapes with
+          // many short items against the per-key index test it replaces).
+          const int lim = (CAUSAL ? min(row, kv_end - 1) : kv_end - 1) - kv0;
 #pragma unroll
-          for (int c = 0; c < BG; ++c) {
-            const int kv = kv0 + c;
-            if (kv >= kv_end || (CAUSAL && kv > row)) s[c] = -INFINITY;
-          }
+          for (int c = 0; c < BG; ++c) s[c] = (c > lim) ? -INFINITY : s[c];
         }
         const float m_new = fmaxf(m_ref, row_max<BG>(s));
         const bool resc = (m_ref == -INFINITY) ? (m_new != -INFINITY)

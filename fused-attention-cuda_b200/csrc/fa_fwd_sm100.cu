@@ -473,11 +473,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         FA_TRACE_EV(rnd == 0 && r == 0, 4, g, t);
         const int kv0 = j * BN;
         if ((CAUSAL && kv0 + BN - 1 > q0) || kv0 + BN > args.N) {
+          // Key kv0 + c is visible to this row iff c <= lim (top-left causal, inside N).
+          const int lim = (CAUSAL ? min(row, args.N - 1) : args.N - 1) - kv0;
 #pragma unroll
-          for (int c = 0; c < BN; ++c) {
-            const int kv = kv0 + c;
-            if (kv >= args.N || (CAUSAL && kv > row)) s[c] = -INFINITY;
-          }
+          for (int c = 0; c < BN; ++c) s[c] = (c > lim) ? -INFINITY : s[c];
         }
         const float m_new = fmaxf(m_ref, row_max<BN>(s));
         const bool resc = (m_ref == -INFINITY) ? (m_new != -INFINITY)
