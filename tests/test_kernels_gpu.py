@@ -438,3 +438,44 @@ def test_input_validation_messages(make_qkv):
             fused_attn.forward_stage(q, k, v, stage)
     with pytest.raises(RuntimeError, match="not implemented|no stage"):
         fused_attn.forward_stage(q.float(), k.float(), v.float(), 5)
+
+
+# ------------------------------------------------------------------------------------------
+def test_launch_past_2_31_elements():
+    """Maximum sizes: q, k, v and o of B65 H16 N16384 D128 fp16 (causal) hold 2.18e9 elements
+    each, so the last heads sit past element offset 2^31 and any 32-bit offset in the tensor
+    maps, the O stores or the LSE index would misplace them.  The first and the last head of the
+    one 17 GB launch equal one-head launches of the same inputs bit for bit (a head's result does
+    not depend on the launch it is in), and the last head matches the oracle on sampled rows
+    (converted to fp64 on the host one head at a time: the whole tensor would not fit)."""
+    require(torch.float16, 128)
+    b, h, n, d = 65, 16, 16384, 128
+    assert b * h * n * d > 2 ** 31
+    need = 4 * b * h * n * d * 2 + b * h * n * 4
+    free, _ = torch.cuda.mem_get_info()
+    if free < need + (4 << 30):
+        pytest.skip(f"needs {need / 2**30:.1f} GiB of device memory, {free / 2**30:.1f} free")
+    try:
+        _check_large_launch(b, h, n, d)
+    finally:
+        torch.cuda.empty_cache()
+
+
+def _check_large_launch(b, h, n, d):
+    g = torch.Generator(device="cuda").manual_seed(5)
+    q, k, v = (torch.randn(b, h, n, d, device="cuda", dtype=torch.float16, generator=g)
+               for _ in range(3))
+    o, lse = fused_attn.forward(q, k, v, is_causal=True, return_lse=True)
+    torch.cuda.synchronize()
+    err, bits = fused_attn.last_device_error()
+    assert err == 0, f"device status {err} bits={bits:#x}"
+    assert bool(torch.isfinite(lse[-1, -1]).all()) and bool(torch.isfinite(o[-1, -1]).all())
+    for bb, hh in ((b - 1, h - 1), (0, 0)):
+        qs, ks, vs = (t[bb:bb + 1, hh:hh + 1].contiguous() for t in (q, k, v))
+        o1, l1 = fused_attn.forward(qs, ks, vs, is_causal=True, return_lse=True)
+        assert torch.equal(o1, o[bb:bb + 1, hh:hh + 1]), (bb, hh)
+        assert torch.equal(l1, lse[bb:bb + 1, hh:hh + 1]), (bb, hh)
+    last = slice(b - 1, b), slice(h - 1, h)
+    qc, kc, vc = (t[last].cpu() for t in (q, k, v))
+    blocks = [(0, 0, 0, 64), (0, 0, n // 2, 64), (0, 0, n - 64, 64)]
+    check_rows(o[last], lse[last], qc, kc, vc, True, torch.float16, blocks)
