@@ -129,3 +129,51 @@ def test_draws_cover_every_kernel_and_layout():
     assert {c["dtype"] for c in cs} == {torch.float16, torch.bfloat16}
     assert {c["causal"] for c in cs} == {True, False}
     assert any(c["scale"] is not None for c in cs) and any(c["mag"] > 1 for c in cs)
+
+
+N_CASES_F32 = 12
+
+
+def draw_f32(case: int) -> dict:
+    rng = random.Random(5000 + case)
+    hkv = rng.choice([1, 2, 4])
+    return {
+        "b": rng.choice([1, 2]),
+        "hkv": hkv,
+        "h": hkv * rng.choice([1, 2]),
+        "n": 32 * rng.randint(1, 24),
+        "d": rng.choice([64, 128]),
+        "causal": rng.random() < 0.5,
+        "scale": rng.choice([None, round(rng.uniform(0.03, 0.4), 4)]),
+        "strided": rng.random() < 0.3,
+        "seed": rng.randint(0, 10**6),
+    }
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", range(N_CASES_F32))
+def test_random_fp32_shape_matches_oracle(case):
+    """fp32 inputs (tf32 tensor cores after the round-to-nearest pre-pass) on random shapes,
+    contiguous or strided: O <= 5e-3 and LSE <= 2e-3 against the oracle (the C1 gates, stated for
+    the default scale 1/sqrt(D)).  tf32 keeps 10 explicit mantissa bits of q and k, so a score's
+    error is relative to the score: at a softmax scale r times the default the scores, and with them
+    the LSE and weight errors, grow r-fold, and both gates are multiplied by max(1, r)."""
+    c = draw_f32(case)
+    if not fused_attn.is_available() or not fused_attn.impl_supports(3, torch.float32, c["d"]):
+        pytest.skip("fp32 path not built")
+    q, k, v = make_qkv(c["b"], c["h"], c["n"], c["d"], dtype=torch.float32, device="cuda",
+                       hkv=c["hkv"], seed=c["seed"])
+    if c["strided"]:
+        qs, ks, vs = (t.transpose(1, 2).contiguous().transpose(1, 2) for t in (q, k, v))
+        o, lse = fused_attn.forward_strided(qs, ks, vs, is_causal=c["causal"], scale=c["scale"],
+                                            return_lse=True)
+    else:
+        o, lse = fused_attn.forward(q, k, v, is_causal=c["causal"], scale=c["scale"],
+                                    return_lse=True)
+    err_dev, bits = fused_attn.last_device_error()
+    assert err_dev == 0, f"device status {err_dev} bits={bits:#x}"
+    o_ref, lse_ref = oracle.attention(q, k, v, causal=c["causal"], scale=c["scale"],
+                                      threads=THREADS)
+    r = 1.0 if c["scale"] is None else max(1.0, c["scale"] * c["d"] ** 0.5)
+    assert oracle.max_abs(o, o_ref) <= 5e-3 * r
+    assert oracle.max_abs(lse, lse_ref) <= 2e-3 * r
